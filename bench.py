@@ -1,0 +1,556 @@
+"""Benchmark of the paged KV-cache store + batch index build on B200.
+
+One step = one pass of the hot path over one batch: the index build of the
+batch (kv_indptr, kv_indices, kv_last_page_len, qo_indptr, slot_mapping) and
+the store of every layer's new K/V rows into the paged pool by that slot
+mapping.  Default workload: Llama-3-8B-shaped decode (32 layers, 8 KV heads x
+128, bf16, page 16), 256 sequences with context U[128, 8192], one new token
+each, a pool of ~150 GB per GPU, randomly fragmented page tables.
+
+With N GPUs (torchrun, one process per GPU) the KV heads are sharded: each
+rank stores 8/N heads of every token into its own head-slice pool, and the
+global batch grows to 256*N sequences, so every rank moves the same bytes
+per step (weak scaling) with no inter-GPU traffic; the index build is
+replicated on each rank.  `value` = store bytes moved by all ranks per step
+(algorithmic: read + write of every K and V row, plus the slots) / the step
+time, max over ranks.
+
+Inputs rotate over R sets of K/V rows and page tables (R * per-step inputs >
+2 x the 126 MB L2, distinct destination slots per set), so neither the reads
+nor the scattered writes are absorbed by L2 between steps.  The timed steps
+run as CUDA-graph replays (the way a serving engine launches a decode step);
+events recorded inside the graphs time every index and store launch.
+
+  python bench.py [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import yllang_b200 as yl  # noqa: E402
+from yllang_b200 import workloads  # noqa: E402
+
+METRIC = "KV-store GB/s (% of HBM peak) + tokens/s stored; index-build µs/batch"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def reduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML polling thread)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons, self.period = [], 0, period_s
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            # NVML enumerates every GPU of the host: find the visible CUDA device by its PCI address
+            pr = torch.cuda.get_device_properties(device_index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report that instead of clocks
+            self.err = repr(e)
+        self._stop = threading.Event()
+
+    def _sample(self):
+        nv = self.nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+        self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+            self._sample()  # at least one sample at the end of the region
+
+    def summary(self) -> dict:
+        if not self.ok:
+            return {"error": getattr(self, "err", "nvml unavailable")}
+        names = [n for n, bit in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": float(statistics.median(self.samples)) if self.samples else None,
+                "sm_max_mhz": float(self.max_mhz), "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workload set-up
+# ---------------------------------------------------------------------------
+def make_batches(name: str, world: int, pool_bytes: int, rotate: int):
+    """R batches of one workload for this rank (same lengths, different pages)."""
+    heads = 8 // world
+    if name == "llama3_decode":
+        layers, ps, row = 32, 16, heads * 128 * 2
+        P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
+        mk = lambda r: workloads.llama3_decode(P, batch=256 * world, kv_heads=heads, seed_pages=2 + r)
+        desc = {"workload": "llama3_8b_decode", "model_shape": "Llama-3-8B", "global_batch": 256 * world,
+                "scaling": "weak"}
+    elif name == "ragged_prefill":
+        layers, ps, row = 32, 16, heads * 128 * 2
+        P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
+        mk = lambda r: workloads.ragged_prefill(P, requests=64 * world, kv_heads=heads, seed_pages=2 + r)
+        desc = {"workload": "ragged_prefill", "global_batch": 64 * world, "scaling": "weak"}
+    elif name == "qwen72b_decode":
+        layers, ps, row = 80, 16, heads * 128 * 2
+        P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
+        mk = lambda r: workloads.qwen72b_decode(P, tp=world, batch=512, seed_pages=2 + r)
+        desc = {"workload": "qwen2_72b_tp_decode", "model_shape": "Qwen2-72B", "global_batch": 512,
+                "scaling": "strong"}
+    elif name.startswith("mixed"):
+        _, ps_s, hd_s = name.split("_")  # mixed_ps16_hd128
+        ps, hd = int(ps_s[2:]), int(hd_s[2:])
+        layers, row = 4, heads * hd * 2
+        P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
+        mk = lambda r: workloads.mixed(P, page_size=ps, head_dim=hd, seed_pages=2 + r)
+        desc = {"workload": name, "global_batch": 136, "scaling": "strong"}
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    batches = [mk(r) for r in range(rotate)]
+    for b in batches:
+        b.kv_heads = heads
+    desc.update(layers=layers, kv_heads_per_gpu=heads, head_dim=batches[0].head_dim, page_size=ps,
+                pool_pages_per_gpu=P, pool_gb_per_gpu=round(2 * layers * P * ps * row / 1e9, 1))
+    return batches, desc
+
+
+class Step:
+    """Device-resident inputs and outputs of one rotation set."""
+
+    def __init__(self, b: workloads.Batch, dev, seed: int):
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
+        self.b = b
+        self.prior, self.new, self.table = t(b.prior_len), t(b.new_len), t(b.page_table)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        E = b.kv_heads * b.head_dim
+        self.k = torch.randn(b.layers, b.tokens, E, generator=g, device=dev, dtype=torch.bfloat16)
+        self.v = torch.randn(b.layers, b.tokens, E, generator=g, device=dev, dtype=torch.bfloat16)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.out = yl.BatchIndex(torch.empty(b.batch + 1, **i32), torch.empty(b.total_pages, **i32),
+                                 torch.empty(b.batch, **i32), torch.empty(b.batch + 1, **i32),
+                                 torch.empty(b.tokens, dtype=torch.int64, device=dev))
+
+    def index(self, err=None):
+        yl.build_index(self.prior, self.new, self.table, self.b.page_size, num_pages=self.b.num_pages,
+                       out=self.out, error_word=err)
+
+    def store(self, k_pool, v_pool, err=None):
+        yl.store_kv_cache(self.k, self.v, k_pool, v_pool, self.out.slot_mapping, error_word=err)
+
+
+def input_bytes(b: workloads.Batch) -> int:
+    """Device bytes of one rotation set's inputs (K/V rows + page table)."""
+    return 2 * b.layers * b.tokens * b.row_bytes + b.page_table.nbytes
+
+
+def plan(args, world, free_bytes):
+    """Pick the rotation count (inputs over 2.2 x L2 unless one set already is)
+    and the pool size (what is left after the inputs, at most --pool-gb)."""
+    probe, _ = make_batches(args.workload, world, 1e9, 1)
+    per_set = input_bytes(probe[0])
+    R = args.rotate if args.rotate > 0 else max(1, min(8, math.ceil(2.2 * L2_BYTES / per_set)))
+    pool_bytes = min(args.pool_gb * 1e9, free_bytes - R * per_set - 12e9)
+    assert pool_bytes > 0, "not enough device memory for the inputs"
+    return R, pool_bytes, per_set
+
+
+def capture(steps, order, k_pool, v_pool, err):
+    """One CUDA graph running the steps in `order`, with a timing event before,
+    between and after the two launches of every step."""
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)] for _ in order]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for j, r in enumerate(order):
+            evs[j][0].record()
+            steps[r].index(err)
+            evs[j][1].record()
+            steps[r].store(k_pool, v_pool, err)
+            evs[j][2].record()
+    return g, evs
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port, all host threads), bounded sample
+# ---------------------------------------------------------------------------
+def cpu_store_step_sample(b: workloads.Batch, seconds: float, threads: int | None = None):
+    """Time the oracle's index build + store of this batch on the host cores
+    for about `seconds`, with the pool scaled down to 4 GB of host memory."""
+    from oracle import kvpath as orc
+
+    threads = threads or orc.max_threads()
+    hb, pool, k, v = host_step_setup(b)
+    host_step(hb, pool, k, v, threads)  # first touch of the pool pages
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        host_step(hb, pool, k, v, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and reps >= 3:
+            break
+    per_step = el / reps
+    gbs = hb.store_bytes() / per_step / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full steps of {hb.name} (B={hb.batch}, N={hb.tokens}, L={hb.layers}, "
+                      f"row {hb.row_bytes} B) into a {pool.nbytes / 1e9:.1f} GB host pool, index build + store, "
+                      f"C oracle on {threads} threads",
+            "ms_per_step": round(per_step * 1e3, 3)}
+
+
+def ref_make2d_us(b: workloads.Batch, max_seconds: float = 5.0):
+    """Time the reference's Make2DIndices (built from its sources, oracle/_ref)
+    producing the decode batch's load indices (page size 1 semantics: one
+    index per context token), on a sample of sequences, scaled to the batch."""
+    import ctypes
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_index.so")
+    if not os.path.exists(path):
+        return None
+    f = ctypes.CDLL(path).ref_make2d_indices
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                  ctypes.POINTER(ctypes.c_int64)]
+    tot = (b.prior_len.astype(np.int64) + b.new_len)
+    W = int(tot.max())
+    done_elems, t0, i = 0, time.perf_counter(), 0
+    while i < b.batch and time.perf_counter() - t0 < max_seconds:
+        rng = np.array([[i * W, 0, int(tot[i])]], np.int64)
+        out = np.zeros(int(tot[i]), np.float32)
+        n = ctypes.c_int64(0)
+        assert f(b.batch, W, rng.ctypes.data, 1, out.ctypes.data, out.size, ctypes.byref(n)) == 0
+        done_elems += int(tot[i])
+        i += 1
+    el = time.perf_counter() - t0
+    return {"us_per_batch": round(el / done_elems * float(tot.sum()) * 1e6, 1), "sampled_sequences": i,
+            "elements_sampled": done_elems, "kind": "reference",
+            "note": "reference Make2DIndices, one libtorch scalar op per element, scaled from the sample"}
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+def host_step_setup(b: workloads.Batch, pool_gb: float = 4.0):
+    """The batch re-drawn for a host pool of pool_gb (same shapes; read-only
+    pages alias, written pages unique) plus its K/V rows as raw bf16 bits."""
+    P = max(workloads.pool_pages_for(pool_gb * 1e9, b.layers, b.row_bytes, b.page_size), b.tokens + 1)
+    if b.name == "llama3_decode":
+        hb = workloads.llama3_decode(P, batch=b.batch, kv_heads=b.kv_heads, layers=b.layers)
+    elif b.name == "ragged_prefill":
+        hb = workloads.ragged_prefill(P, requests=b.batch, kv_heads=b.kv_heads, layers=b.layers)
+    else:
+        hb = b
+    S = hb.num_pages * hb.page_size
+    E = hb.kv_heads * hb.head_dim
+    pool = np.zeros((2, hb.layers, S, E), np.uint16)
+    rng = np.random.default_rng(0)
+    k = rng.integers(0, 1 << 16, (hb.layers, hb.tokens, E), dtype=np.uint16)
+    v = rng.integers(0, 1 << 16, (hb.layers, hb.tokens, E), dtype=np.uint16)
+    return hb, pool, k, v
+
+
+def host_step(hb, pool, k, v, threads):
+    from oracle import kvpath as orc
+    out = orc.build_index(hb.prior_len, hb.new_len, hb.page_table, hb.page_size, num_pages=hb.num_pages)
+    orc.store(k, v, pool[0], pool[1], out["slot_mapping"], num_slots=pool.shape[2], threads=threads)
+
+
+def run_reference(args, world, rank):
+    """CPU arm: the path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    from oracle import kvpath as orc
+    batches, desc = make_batches(args.workload, 1, 150e9, 1)
+    b = batches[0]
+    threads = orc.max_threads()
+    hb, pool, k, v = host_step_setup(b)
+    times = []
+    for it in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        host_step(hb, pool, k, v, threads)
+        if it >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    per = sum(times) / len(times)
+    gbs = hb.store_bytes() / per / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 4), "higher_is_better": True,
+        "scaling": desc.get("scaling", "weak"), "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded lengths and fragmented page tables, random bf16 bit patterns",
+        "config": desc,
+        "tokens_per_s": round(hb.tokens / per, 1),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"each step: index build + store of {hb.name} (B={hb.batch}, N={hb.tokens}, "
+                                   f"L={hb.layers}) into a {pool.nbytes / 1e9:.1f} GB host pool by the C oracle; "
+                                   "the reference's store exists only as a CUDA kernel"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    mk = ref_make2d_us(b, max_seconds=5.0)
+    if mk:
+        line["reference_make2dindices"] = mk
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    dev = torch.device("cuda", local)
+    free, total = torch.cuda.mem_get_info(dev)
+    R, pool_bytes, per_set = plan(args, world, free)
+    batches, desc = make_batches(args.workload, world, pool_bytes, R)
+    b0 = batches[0]
+    P = b0.num_pages
+    S = P * b0.page_size
+    E = b0.kv_heads * b0.head_dim
+    L = b0.layers
+    pool = torch.empty((2, L, S, E), dtype=torch.bfloat16, device=dev)
+    k_pool, v_pool = pool[0], pool[1]
+    steps = [Step(b, dev, seed=1000 * rank + r) for r, b in enumerate(batches)]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    store_bytes = b0.store_bytes()
+    index_bytes = b0.index_bytes()
+    in_bytes_per_set = per_set
+    two_launch = b0.batch > 16384
+    launches_per_step = 3 if two_launch else 2
+
+    # warm-up: eager steps through the public API
+    for w in range(args.warmup):
+        s = steps[w % R]
+        s.index(err)
+        s.store(k_pool, v_pool, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, f"device error word {int(err.item()):#x} during warm-up"
+
+    # graphs: chunk of C steps replayed q times + remainder, events per launch
+    K = args.steps
+    C = min(K, args.chunk)
+    q, rem = divmod(K, C)
+    g_main, ev_main = capture(steps, [j % R for j in range(C)], k_pool, v_pool, err)
+    g_rem, ev_rem = (capture(steps, [(q * C + j) % R for j in range(rem)], k_pool, v_pool, err)
+                     if rem else (None, []))
+    g_main.replay()  # untimed graph warm-up
+    torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(q):
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    ms_max = reduce_max(ms, world)
+    idx_ms = [e[0].elapsed_time(e[1]) for e in ev_main + ev_rem]
+    st_ms = [e[1].elapsed_time(e[2]) for e in ev_main + ev_rem]
+    assert int(err.item()) == 0, f"device error word {int(err.item()):#x}"
+
+    per_step_s = ms_max / 1e3 / K
+    total_store = reduce_sum(float(store_bytes), world)
+    value = total_store / per_step_s / 1e9
+    tokens_global = b0.tokens  # every rank stores its head slice of every token
+    store_us = statistics.mean(st_ms) * 1e3
+    index_us = statistics.mean(idx_ms) * 1e3
+    peak, peak_kind = load_peaks()
+    achieved = store_bytes / (store_us * 1e-6) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        if per_set <= 4e9:
+            e2e = run_e2e(args, steps[:min(R, 2)], k_pool, v_pool, err, world)
+        else:
+            e2e = {"value": None, "unit": "GB/s", "skipped": f"one step's inputs are {per_set / 1e9:.0f} GB"}
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
+            "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded lengths and fragmented page tables, K/V N(0,1) cast to bf16",
+            "config": dict(desc, parallelism=f"kv-head shard x{world}" if world > 1 else "single GPU",
+                           l2=f"inputs rotate over {R} sets ({R * in_bytes_per_set / 1e6:.0f} MB > 2 x L2), "
+                              "distinct destination slots per set"),
+            "tokens_per_s": round(tokens_global / per_step_s, 1),
+            "pct_hbm": round(100 * value / (peak * world), 2),
+            "store_us": round(store_us, 3), "index_build_us": round(index_us, 3),
+            "store_gbs": round(achieved, 1),
+            "index_gbs": round(index_bytes / (index_us * 1e-6) / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": args.traffic,
+                         "kernel": "store_rows_kernel", "peak_source": f"{peak_kind} hbm_gbs (copy)",
+                         "algorithmic_bytes_per_launch": store_bytes},
+            "gpu_launches": launches_per_step * K,
+            "clocks": clocks.summary(),
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_store_step_sample(b0, seconds=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del g_main, g_rem
+
+
+def run_e2e(args, steps, k_pool, v_pool, err, world):
+    """The same step through the public API with host inputs: every step
+    copies its K/V rows, lengths and page table from pinned host memory,
+    builds the index, stores, and reads the error word back."""
+    R = len(steps)
+    dev = steps[0].k.device
+    host = []
+    for s in steps:
+        host.append({n: getattr(s, n).cpu().pin_memory() for n in ("k", "v", "prior", "new", "table")})
+    dk = {n: torch.empty_like(getattr(steps[0], n)) for n in ("k", "v", "prior", "new", "table")}
+    out = steps[0].out
+    err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    E = min(args.steps, args.e2e_steps)
+    b = steps[0].b
+
+    def one(r):
+        h = host[r]
+        for n in dk:
+            if dk[n].shape != h[n].shape:
+                dk[n] = torch.empty(h[n].shape, dtype=h[n].dtype, device=dev)
+            dk[n].copy_(h[n], non_blocking=True)
+        yl.build_index(dk["prior"], dk["new"], dk["table"], b.page_size, num_pages=b.num_pages, out=out,
+                       error_word=err)
+        yl.store_kv_cache(dk["k"], dk["v"], k_pool, v_pool, out.slot_mapping, error_word=err)
+        err_host.copy_(err, non_blocking=True)
+
+    for r in range(min(3, R)):
+        one(r)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for j in range(E):
+        one(j % R)
+    end.record()
+    torch.cuda.synchronize()
+    ms = reduce_max(start.elapsed_time(end), world)
+    h2d = sum(host[0][n].nbytes for n in ("k", "v", "prior", "new", "table"))
+    per = ms / 1e3 / E
+    total = reduce_sum(float(b.store_bytes()), world)
+    return {"value": round(total / per / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": 4, "steps": E, "ms_per_step": round(ms / E, 4),
+            "path": "pinned host -> device copies, yllang_b200.build_index + store_kv_cache, error word -> host"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="llama3_decode")
+    ap.add_argument("--rotate", type=int, default=0, help="input sets cycled through (0: enough to exceed 2.2 x L2)")
+    ap.add_argument("--chunk", type=int, default=256, help="steps per captured CUDA graph")
+    ap.add_argument("--pool-gb", type=float, default=150.0)
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu DRAM bytes per store launch (from the committed profile) to report")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)  # at least three untimed steps
+    world, rank, local = dist_setup()
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,188 @@
+/*
+ * yl_kvpath.h — C ABI of the B200 paged KV-cache store and batch index build.
+ *
+ * Two hot operations of an LLM serving step, as hand-written sm_100a CUDA:
+ *
+ *   yl_kv_store     scatter each step's new K/V rows into the paged pool by
+ *                   slot mapping (replaces yllang::StoreKVCache,
+ *                   src/kvcache/store_kv_cache.cu:95-163, declared at
+ *                   src/include/kvcache/store_kv_cache.h:29-31, and the call in
+ *                   MHAKVCache::StoreKV, src/include/kvcache/mha_kvcache.h:76-86).
+ *
+ *   yl_build_index  build the paged-attention page arrays of one batch
+ *                   (kv_indptr, kv_indices, kv_last_page_len, qo_indptr,
+ *                   slot_mapping) from per-sequence lengths and page-table rows
+ *                   (replaces the load/write index construction of
+ *                   BatchManager::NextBatch, src/include/batch/batch_manager.h:83-115,
+ *                   and Make2DIndices, batch_manager.h:30-51).
+ *
+ * Every pointer in an argument struct is a DEVICE pointer unless stated
+ * otherwise; every stride and size is in BYTES unless its name says
+ * "elements".  Calls are asynchronous on the given stream (NULL = legacy
+ * default stream), allocate nothing and never synchronise.  A call returns
+ * YL_OK or a negative yl_status; no C++ exception crosses this boundary.
+ * Argument errors are detected on the host before any launch.  Data errors
+ * that only the device can see (a slot or page id out of range, a page-table
+ * row too short, an output buffer too small) skip the offending element and
+ * set a bit in the caller's optional device error word (see YL_DEVERR_*);
+ * kernels never trap.
+ */
+#ifndef YL_KVPATH_H_
+#define YL_KVPATH_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as the CUDA runtime's cudaStream_t (an opaque CUstream_st*). */
+struct CUstream_st;
+typedef struct CUstream_st *cudaStream_t;
+
+#define YL_KVPATH_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define YL_API __attribute__((visibility("default")))
+#else
+#define YL_API
+#endif
+
+/* Host-side status codes returned by every entry point. */
+typedef enum yl_status {
+  YL_OK = 0,
+  YL_ERR_NULL_ARG = -1,     /* a required pointer is NULL                        */
+  YL_ERR_BAD_SIZE = -2,     /* negative count, zero/negative row size, ...       */
+  YL_ERR_ALIGNMENT = -3,    /* pointer/stride not a multiple of the element unit */
+  YL_ERR_UNSUPPORTED = -4,  /* a combination this build does not implement       */
+  YL_ERR_CUDA = -5          /* the CUDA runtime refused the launch               */
+} yl_status;
+
+/* Bits a kernel ORs into the caller's device error word. */
+#define YL_DEVERR_SLOT_RANGE      0x1u  /* store: slot >= num_slots or < -1 (row skipped)   */
+#define YL_DEVERR_PAGE_RANGE      0x2u  /* index: page id outside [0, num_pages)            */
+#define YL_DEVERR_ROW_OVERFLOW    0x4u  /* index: a sequence needs more pages than its row  */
+#define YL_DEVERR_INDICES_CAP     0x8u  /* index: sum of pages exceeds kv_indices_capacity  */
+#define YL_DEVERR_SLOTS_CAP       0x10u /* index: sum of new tokens exceeds slot_capacity   */
+#define YL_DEVERR_NEGATIVE_LEN    0x20u /* index: a negative length (treated as 0)          */
+#define YL_DEVERR_INDPTR_OVERFLOW 0x40u /* index: a running sum passed INT32_MAX (no fill)  */
+#define YL_DEVERR_TABLE_ROW       0x80u /* index: table_index outside [0, num_table_rows)   */
+
+/*
+ * Store (replaces yllang::StoreKVCache<kElementSize>,
+ * src/kvcache/store_kv_cache.cu:95-163, and its kernel StoreKVCacheKernel,
+ * store_kv_cache.cu:46-77).
+ *
+ * For every layer l < num_layers and token i < num_tokens:
+ *     row(k_cache, l, slots[i]) <- row(k, l, i)
+ *     row(v_cache, l, slots[i]) <- row(v, l, i)
+ * where row(base, l, r) is the row_bytes bytes at
+ *     base + l * <layer stride> + r * <row stride>.
+ * The copy is bit-exact and dtype-agnostic.  With num_layers == 1 this is the
+ * reference's per-layer call; num_layers > 1 stores every layer of one step in
+ * one launch (inputs laid out [L, N, row] with the given strides, pool laid
+ * out layer-major as MHAKVCache allocates it, mha_kvcache.h:42-62).
+ *
+ * Slots are int32 or int64 (slot_is_int64).  The reference always reads
+ * int64 (store_kv_cache.cu:127 compares bytes with bits); here both work.
+ * A slot of -1 marks a padding token and is skipped silently.  When
+ * num_slots > 0, a slot outside [-1, num_slots) skips its row and sets
+ * YL_DEVERR_SLOT_RANGE.  Duplicate slots inside one call are outside the
+ * contract (as in the reference, the winner is unspecified); across calls on
+ * one stream the later call wins.  num_tokens == 0 is a no-op
+ * (mha_kvcache.h:77-79).
+ *
+ * Alignment: the widest unit u in {16, 8, 4, 2, 1} bytes that divides
+ * row_bytes, every base pointer and every stride is used; the fast paths need
+ * u == 16 (bf16/fp16 rows of H*D a multiple of 8 elements, fp32 of 4).
+ */
+typedef struct yl_store_args {
+  const void *k;              /* input K rows of layer 0                          */
+  const void *v;              /* input V rows of layer 0                          */
+  void *k_cache;              /* K pool of layer 0, viewed as [num_slots, row]    */
+  void *v_cache;              /* V pool of layer 0                                */
+  const void *slots;          /* [num_tokens] int32 or int64 slot mapping          */
+  int32_t slot_is_int64;      /* 0: int32 slots, 1: int64 slots                   */
+  int32_t num_layers;         /* >= 1                                             */
+  int64_t num_tokens;         /* >= 0                                             */
+  int64_t row_bytes;          /* bytes of one token's row (H_local*D*dtype size)  */
+  int64_t k_row_stride;       /* bytes between consecutive tokens of k            */
+  int64_t v_row_stride;       /* bytes between consecutive tokens of v            */
+  int64_t cache_row_stride;   /* bytes between consecutive slots of either pool   */
+  int64_t k_layer_stride;     /* bytes between layers of k (ignored if L == 1)    */
+  int64_t v_layer_stride;     /* bytes between layers of v                        */
+  int64_t cache_layer_stride; /* bytes between layers of either pool              */
+  int64_t num_slots;          /* slots per layer for range checks; <= 0: no check */
+  uint32_t *error_word;       /* optional device word for YL_DEVERR_* bits        */
+} yl_store_args;
+
+YL_API int yl_kv_store(const yl_store_args *args, cudaStream_t stream);
+
+/*
+ * Index build (replaces the index construction of BatchManager::NextBatch,
+ * src/include/batch/batch_manager.h:83-115, and Make2DIndices,
+ * batch_manager.h:30-51, generalised from page_size 1 to any page size; the
+ * output is the paged-KV page-table format a flashinfer paged-attention
+ * call consumes).
+ *
+ * Per sequence i < batch_size, with row_i = table_index ? table_index[i] : i,
+ * P_i[j] = page_table[row_i * page_table_stride + j], total_i =
+ * prior_len[i] + new_len[i] and np_i = ceil(total_i / page_size):
+ *     kv_indptr[0] = 0,  kv_indptr[i+1] = kv_indptr[i] + np_i
+ *     kv_indices[kv_indptr[i] + j] = P_i[j]                  (j < np_i)
+ *     kv_last_page_len[i] = (total_i - 1) % page_size + 1    (0 if total_i == 0)
+ *     qo_indptr[0] = 0,  qo_indptr[i+1] = qo_indptr[i] + new_len[i]
+ *     slot_mapping[qo_indptr[i] + t] = P_i[p / page_size] * page_size + p % page_size,
+ *         p = prior_len[i] + t                               (t < new_len[i])
+ * prior_len plays the role of Request::CachedLen and prior_len + new_len of
+ * Request::DeviceLen (src/include/request/request.h:81-92).
+ *
+ * Checks on the device (each skips the element and sets its error bit):
+ * np_i > max_pages_per_row (the sequence keeps max_pages_per_row pages and
+ * its slots past them are written as -1), page ids outside [0, num_pages)
+ * when num_pages > 0 (kv_indices keeps the id, the slot is written as -1),
+ * table_index outside [0, num_table_rows) (the sequence gets no pages and
+ * -1 slots), sum of np_i > kv_indices_capacity, sum of new_len >
+ * slot_capacity, negative lengths (treated as 0).
+ * Any outputs except kv_indptr/qo_indptr may be NULL to skip them.
+ */
+typedef struct yl_index_args {
+  const int32_t *prior_len;     /* [B] tokens already in the pool               */
+  const int32_t *new_len;       /* [B] tokens stored this step                  */
+  const int32_t *page_table;    /* 2-D page table, int32 page ids               */
+  const int32_t *table_index;   /* [B] page-table row per sequence, or NULL     */
+  int64_t page_table_stride;    /* ELEMENTS between page-table rows             */
+  int32_t num_table_rows;       /* rows of page_table; > 0 required with        */
+                                /* table_index; without it rows 0..B-1 are used */
+                                /* (checked against this count when > 0)        */
+  int32_t max_pages_per_row;    /* page-table columns usable by a sequence      */
+  int32_t page_size;            /* tokens per page, >= 1                        */
+  int32_t batch_size;           /* B >= 0                                       */
+  int32_t slot_is_int64;        /* element type of slot_mapping                 */
+  int64_t num_pages;            /* pool pages for range checks; <= 0: no check  */
+  int32_t *kv_indptr;           /* [B+1]                                        */
+  int32_t *kv_indices;          /* [kv_indices_capacity]                        */
+  int32_t *kv_last_page_len;    /* [B]                                          */
+  int32_t *qo_indptr;           /* [B+1]                                        */
+  void *slot_mapping;           /* [slot_capacity] int32 or int64               */
+  int64_t kv_indices_capacity;  /* elements available in kv_indices             */
+  int64_t slot_capacity;        /* elements available in slot_mapping           */
+  uint32_t *error_word;         /* optional device word for YL_DEVERR_* bits    */
+} yl_index_args;
+
+YL_API int yl_build_index(const yl_index_args *args, cudaStream_t stream);
+
+/* Human-readable name of a yl_status value (static storage). */
+YL_API const char *yl_status_string(int status);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+YL_API const char *yl_last_error(void);
+
+/* YL_KVPATH_ABI_VERSION of the loaded library. */
+YL_API int yl_abi_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* YL_KVPATH_H_ */

@@ -1,0 +1,181 @@
+"""Python face of the CPU oracle for the paged KV store and batch index build.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by ``__graft_entry__.smoke()``
+as the checker, and by bench.py's CPU-baseline leg.  The product package
+(``yllang_b200``) never imports it.
+
+Two restatements of the reference's algorithm live here:
+
+* the C oracle (``kvpath_oracle.c``, built into ``liboracle_kvpath.so``), the
+  one the tests and the CPU baseline use;
+* pure-Python loops (``py_store`` / ``py_build_index``) for small cases, a
+  second, independent statement used to cross-check the C one.
+
+The store follows StoreKVCacheKernel (src/kvcache/store_kv_cache.cu:60-72) as
+driven by MHAKVCache::StoreKV (src/include/kvcache/mha_kvcache.h:76-86); the
+index build follows the request ranges of BatchManager::NextBatch
+(src/include/batch/batch_manager.h:97-112) generalised to page_size >= 1.
+Argument meanings and error bits are those of include/yl_kvpath.h.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle_kvpath.so")
+_lib = None
+
+SLOT_RANGE = 0x1
+PAGE_RANGE = 0x2
+ROW_OVERFLOW = 0x4
+INDICES_CAP = 0x8
+SLOTS_CAP = 0x10
+NEGATIVE_LEN = 0x20
+INDPTR_OVERFLOW = 0x40
+TABLE_ROW = 0x80
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+
+
+def build(with_reference: bool = False) -> None:
+    """Compile the oracle (and, if asked and present, the reference checkers)."""
+    target = ["all", "ref"] if with_reference else ["all"]
+    env = dict(os.environ)
+    # The C oracle is plain C11 + pthreads: any gcc works.
+    env.setdefault("CC", "gcc")
+    subprocess.run(["make", "-s", "-C", _HERE, *target], check=True, env=env)
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.oracle_kv_store.restype = _i64
+        L.oracle_kv_store.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i32,
+                                      _i64, _i64, _i64, _i64, _vp, ctypes.c_int]
+        L.oracle_build_index.restype = ctypes.c_int
+        L.oracle_build_index.argtypes = [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp,
+                                         _vp, ctypes.c_int, _i64, _i64, _vp]
+        L.oracle_max_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def max_threads() -> int:
+    return int(lib().oracle_max_threads())
+
+
+def _ptr(a: np.ndarray | None) -> int | None:
+    return None if a is None else a.ctypes.data
+
+
+def _as3(a: np.ndarray) -> np.ndarray:
+    return a[None] if a.ndim == 2 else a
+
+
+def store(k: np.ndarray, v: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, slots: np.ndarray,
+          num_slots: int = 0, threads: int = 1) -> tuple[int, int]:
+    """Scatter K/V rows into the caches in place; returns (rows copied, error bits).
+
+    k, v: [N, E] or [L, N, E]; k_cache, v_cache: [S, E] or [L, S, E] (the
+    pool's per-layer [pages * page_size, H * D] views); any dtype, rows must be
+    contiguous in their last axis; slots int32 or int64 [N].
+    """
+    k3, v3, kc3, vc3 = _as3(k), _as3(v), _as3(k_cache), _as3(v_cache)
+    L, N, E = k3.shape
+    if N == 0:  # MHAKVCache::StoreKV returns early (mha_kvcache.h:77-79)
+        return 0, 0
+    item = k3.itemsize
+    for a in (k3, v3, kc3, vc3):
+        assert a.strides[2] == item and a.shape[2] == E and a.itemsize == item
+    assert kc3.strides == vc3.strides and kc3.shape == vc3.shape and v3.shape == k3.shape
+    assert slots.dtype in (np.int32, np.int64) and slots.shape == (N,) and slots.flags.c_contiguous
+    err = ctypes.c_uint32(0)
+    copied = lib().oracle_kv_store(
+        _ptr(k3), _ptr(v3), _ptr(kc3), _ptr(vc3), _ptr(slots), int(slots.dtype == np.int64), N, E * item,
+        k3.strides[1], v3.strides[1], kc3.strides[1], L, k3.strides[0], v3.strides[0], kc3.strides[0],
+        int(num_slots), ctypes.addressof(err), int(threads))
+    return int(copied), int(err.value)
+
+
+def build_index(prior_len, new_len, page_table: np.ndarray, page_size: int, table_index=None, num_pages: int = 0,
+                max_pages_per_row: int | None = None, slot_dtype=np.int64, kv_indices_capacity: int | None = None,
+                slot_capacity: int | None = None) -> dict:
+    """Index build on the host.  Returns the five arrays plus 'err' and 'rc'."""
+    prior = np.ascontiguousarray(prior_len, dtype=np.int32)
+    fresh = np.ascontiguousarray(new_len, dtype=np.int32)
+    B = prior.shape[0]
+    pt = np.ascontiguousarray(page_table, dtype=np.int32)
+    if pt.ndim == 1:
+        pt = pt[None]
+    tix = None if table_index is None else np.ascontiguousarray(table_index, dtype=np.int32)
+    mppr = pt.shape[1] if max_pages_per_row is None else max_pages_per_row
+    tot = prior.astype(np.int64).clip(min=0) + fresh.astype(np.int64).clip(min=0)
+    if kv_indices_capacity is None:
+        kv_indices_capacity = int(np.minimum((tot + page_size - 1) // page_size, mppr).sum()) if B else 0
+    if slot_capacity is None:
+        slot_capacity = int(fresh.astype(np.int64).clip(min=0).sum())
+    out = {
+        "kv_indptr": np.zeros(B + 1, np.int32),
+        "kv_indices": np.zeros(max(kv_indices_capacity, 1), np.int32),
+        "kv_last_page_len": np.zeros(max(B, 1), np.int32),
+        "qo_indptr": np.zeros(B + 1, np.int32),
+        "slot_mapping": np.zeros(max(slot_capacity, 1), slot_dtype),
+    }
+    err = ctypes.c_uint32(0)
+    rc = lib().oracle_build_index(
+        _ptr(prior), _ptr(fresh), _ptr(pt), _ptr(tix), pt.strides[0] // 4, pt.shape[0], mppr, page_size, B,
+        int(num_pages), _ptr(out["kv_indptr"]), _ptr(out["kv_indices"]), _ptr(out["kv_last_page_len"]),
+        _ptr(out["qo_indptr"]), _ptr(out["slot_mapping"]), int(np.dtype(slot_dtype) == np.int64),
+        kv_indices_capacity, slot_capacity, ctypes.addressof(err))
+    out["kv_indices"] = out["kv_indices"][:kv_indices_capacity]
+    out["kv_last_page_len"] = out["kv_last_page_len"][:B]
+    out["slot_mapping"] = out["slot_mapping"][:slot_capacity]
+    out["err"] = int(err.value)
+    out["rc"] = int(rc)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Pure-Python restatement (small cases only).
+# ---------------------------------------------------------------------------
+def py_store(k, v, k_cache, v_cache, slots) -> None:
+    """Row-by-row copy, last writer wins: k_cache[l, slots[i]] = k[l, i]."""
+    k3, v3, kc3, vc3 = _as3(k), _as3(v), _as3(k_cache), _as3(v_cache)
+    for layer in range(k3.shape[0]):
+        for i, s in enumerate(slots.tolist()):
+            if s < 0:
+                continue
+            kc3[layer, s] = k3[layer, i]
+            vc3[layer, s] = v3[layer, i]
+
+
+def py_build_index(prior_len, new_len, page_table, page_size, table_index=None):
+    """Straight loops over the formulas of the index contract (valid inputs)."""
+    kv_indptr, kv_indices, last, qo_indptr, slots = [0], [], [], [0], []
+    for i, (p, n) in enumerate(zip(list(prior_len), list(new_len))):
+        row = i if table_index is None else int(table_index[i])
+        total = int(p) + int(n)
+        pages = -(-total // page_size)
+        kv_indices += [int(x) for x in page_table[row][:pages]]
+        kv_indptr.append(kv_indptr[-1] + pages)
+        last.append(0 if total == 0 else (total - 1) % page_size + 1)
+        qo_indptr.append(qo_indptr[-1] + int(n))
+        for t in range(int(n)):
+            pos = int(p) + t
+            slots.append(int(page_table[row][pos // page_size]) * page_size + pos % page_size)
+    return {
+        "kv_indptr": np.array(kv_indptr, np.int32),
+        "kv_indices": np.array(kv_indices, np.int32),
+        "kv_last_page_len": np.array(last, np.int32),
+        "qo_indptr": np.array(qo_indptr, np.int32),
+        "slot_mapping": np.array(slots, np.int64),
+    }

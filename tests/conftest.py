@@ -1,0 +1,20 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); runs the sm_100a kernels")
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+
+    assert torch.cuda.is_available(), "gpu-marked test run without a CUDA device"
+    return torch.device("cuda:0")

@@ -1,0 +1,173 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, its structs match the ctypes binding byte for byte, argument
+errors come back as status codes before any launch, and the multiply-shift
+divider used by the kernels is exact."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import yllang_b200 as yl
+from yllang_b200 import _abi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "yl_kvpath.h")
+
+
+def _declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"YL_API\s+[\w\s\*]*?\b(yl_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = yl.lib()
+    declared = _declared_symbols()
+    assert declared == sorted(_abi.EXPORTED_SYMBOLS)
+    for name in declared:
+        assert hasattr(L, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", _abi.LIB_PATH], capture_output=True, text=True, check=True)
+    exported = sorted(set(re.findall(r" T (yl_\w+)", out.stdout)))
+    assert exported == declared
+    assert L.yl_abi_version() == _abi.ABI_VERSION
+
+
+def _c_layout(tmp_path, struct, fields):
+    src = tmp_path / "layout.c"
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "yl_kvpath.h"', "int main(void) {",
+             f'  printf("size %zu\\n", sizeof({struct}));']
+    for f in fields:
+        lines.append(f'  printf("{f} %zu\\n", offsetof({struct}, {f}));')
+    lines += ["  return 0;", "}"]
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{os.path.dirname(HEADER)}", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    return {k: int(v) for k, v in (line.split() for line in out.strip().splitlines())}
+
+
+@pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs)])
+def test_struct_layout_matches_header(tmp_path, struct, cls):
+    names = [f for f, _ in cls._fields_]
+    c = _c_layout(tmp_path, struct, names)
+    assert c["size"] == ctypes.sizeof(cls)
+    for f in names:
+        assert c[f] == getattr(cls, f).offset, f
+
+
+def _store(**kw):
+    a = _abi.StoreArgs()
+    base = dict(k=0x1000, v=0x2000, k_cache=0x10000, v_cache=0x20000, slots=0x3000, slot_is_int64=1, num_layers=1,
+                num_tokens=4, row_bytes=256, k_row_stride=256, v_row_stride=256, cache_row_stride=256)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(num_tokens=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(num_layers=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(row_bytes=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(k=0), _abi.YL_ERR_NULL_ARG),
+    (dict(slots=0), _abi.YL_ERR_NULL_ARG),
+    (dict(slot_is_int64=2), _abi.YL_ERR_BAD_SIZE),
+    (dict(cache_row_stride=128), _abi.YL_ERR_BAD_SIZE),
+    (dict(slots=0x3004), _abi.YL_ERR_ALIGNMENT),
+    (dict(num_layers=1 << 20, num_tokens=1 << 12), _abi.YL_ERR_UNSUPPORTED),
+])
+def test_store_rejects_bad_arguments_on_host(kw, status):
+    assert _abi.kv_store_raw(_store(**kw), None) == status
+    assert _abi.last_error().startswith("yl_kv_store")
+
+
+def test_store_zero_tokens_is_noop_without_device():
+    # MHAKVCache::StoreKV returns before any launch when N == 0 (mha_kvcache.h:77-79)
+    assert _abi.kv_store_raw(_store(num_tokens=0, k=0, v=0, slots=0), None) == _abi.YL_OK
+    assert yl.lib().yl_kv_store(None, None) == _abi.YL_ERR_NULL_ARG
+    assert yl.lib().yl_build_index(None, None) == _abi.YL_ERR_NULL_ARG
+
+
+def _index(**kw):
+    a = _abi.IndexArgs()
+    base = dict(prior_len=0x1000, new_len=0x2000, page_table=0x3000, page_table_stride=8, num_table_rows=4,
+                max_pages_per_row=8, page_size=16, batch_size=4, slot_is_int64=1, kv_indptr=0x4000,
+                kv_indices=0x5000, kv_last_page_len=0x6000, qo_indptr=0x7000, slot_mapping=0x8000,
+                kv_indices_capacity=32, slot_capacity=32)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(batch_size=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(page_size=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(kv_indptr=0), _abi.YL_ERR_NULL_ARG),
+    (dict(qo_indptr=0), _abi.YL_ERR_NULL_ARG),
+    (dict(prior_len=0), _abi.YL_ERR_NULL_ARG),
+    (dict(page_table=0), _abi.YL_ERR_NULL_ARG),
+    (dict(table_index=0x9000, num_table_rows=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(num_table_rows=2), _abi.YL_ERR_BAD_SIZE),
+    (dict(kv_indices_capacity=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(slot_mapping=0x8004), _abi.YL_ERR_ALIGNMENT),
+    (dict(max_pages_per_row=-1), _abi.YL_ERR_BAD_SIZE),
+])
+def test_index_rejects_bad_arguments_on_host(kw, status):
+    assert _abi.build_index_raw(_index(**kw), None) == status
+    assert _abi.last_error().startswith("yl_build_index")
+
+
+def test_status_strings():
+    assert _abi.status_string(0) == "YL_OK"
+    assert _abi.status_string(-3) == "YL_ERR_ALIGNMENT"
+    with pytest.raises(yl.KVPathError, match="YL_ERR_BAD_SIZE"):
+        _abi.check(_abi.kv_store_raw(_store(num_tokens=-1), None))
+
+
+def test_launch_without_device_reports_cuda_error():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    # valid arguments, no GPU: the launch must fail with a status, not crash
+    assert _abi.kv_store_raw(_store(), None) == _abi.YL_ERR_CUDA
+
+
+FASTDIV_PROBE = r"""
+#include <cstdio>
+#include <cstdint>
+#include "common.cuh"
+int main() {
+  const uint32_t divs[] = {1, 2, 3, 5, 7, 16, 17, 64, 100, 255, 256, 257, 1000, 4096, 65535, 65536, 65537,
+                           1000003, 123456789, 1u << 30, (1u << 30) + 1, 2147483647u};
+  const uint32_t nums[] = {0, 1, 2, 3, 15, 16, 17, 255, 256, 65535, 65536, 999999, 1u << 20, 123456789,
+                           1u << 30, (1u << 30) + 7, 2147483646u, 2147483647u};
+  long bad = 0;
+  for (uint32_t d : divs) {
+    ylk::FastDiv f(d);
+    for (uint32_t n : nums) if (f.div(n) != n / d) ++bad;
+    for (uint32_t n = 0; n < 200000; ++n) if (f.div(n) != n / d) ++bad;
+    for (uint32_t q = 1; q < 4096; ++q) {               // around multiples of d
+      const uint64_t m = (uint64_t)q * d;
+      for (int dd = -1; dd <= 1; ++dd) {
+        const uint64_t n = m + dd;
+        if (n < (1ull << 31) && f.div((uint32_t)n) != (uint32_t)n / d) ++bad;
+      }
+    }
+  }
+  printf("%ld\n", bad);
+  return 0;
+}
+"""
+
+
+def test_fastdiv_exact(tmp_path):
+    src = tmp_path / "fastdiv.cu"
+    src.write_text(FASTDIV_PROBE)
+    exe = tmp_path / "fastdiv"
+    csrc = os.path.join(ROOT, "yllang_b200", "csrc")
+    subprocess.run(["nvcc", "-std=c++17", "-O2", f"-I{csrc}", f"-I{os.path.dirname(HEADER)}", str(src), "-o",
+                    str(exe)], check=True)
+    assert subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.strip() == "0"

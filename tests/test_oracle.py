@@ -1,0 +1,183 @@
+"""Pin the CPU oracle before trusting it (no GPU needed).
+
+* index build vs golden vectors produced by the reference's own
+  Make2DIndices (tests/golden/index_ps1_*.json, made by make_index_golden.py);
+* index build vs the known answers of the five-request page-size-16 batch;
+* C oracle vs the independent pure-Python restatement on seeded random cases;
+* store semantics ported from the reference's test/mha_kvcache_test.cpp.
+"""
+import glob
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import kvpath as orc
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "index_ps1_*.json"))))
+def test_index_oracle_matches_reference_make2dindices(path):
+    d = json.load(open(path))
+    pt = np.array(d["page_table"], np.int32)
+    out = orc.build_index(d["prior_len"], d["new_len"], pt, d["page_size"], table_index=d["table_index"])
+    assert out["err"] == 0 and out["rc"] == 0
+    assert out["kv_indptr"].tolist() == d["kv_indptr"]
+    assert out["kv_indices"].tolist() == d["kv_indices"]
+    assert out["qo_indptr"].tolist() == d["qo_indptr"]
+    assert out["slot_mapping"].tolist() == d["slot_mapping"]
+    # page size 1: every non-empty sequence's last page holds one token
+    tot = np.array(d["prior_len"]) + np.array(d["new_len"])
+    assert out["kv_last_page_len"].tolist() == [1 if t else 0 for t in tot]
+
+
+def test_index_oracle_known_answers_page16():
+    # priors 17/33/64/100 with one decode token each, plus a 48-token prefill
+    prior = [17, 33, 64, 100, 0]
+    fresh = [1, 1, 1, 1, 48]
+    W = 8
+    pages = (np.arange(5 * W, dtype=np.int32) * 7 + 3).reshape(5, W)
+    out = orc.build_index(prior, fresh, pages, 16, num_pages=1024)
+    assert out["err"] == 0
+    assert out["kv_indptr"].tolist() == [0, 2, 5, 10, 17, 20]
+    assert out["kv_last_page_len"].tolist() == [2, 2, 1, 5, 16]
+    assert out["qo_indptr"].tolist() == [0, 1, 2, 3, 4, 52]
+    s = out["slot_mapping"]
+    assert s.shape == (52,)
+    assert s[0] == pages[0][1] * 16 + 1          # seq 0: position 17
+    assert s[2] == pages[2][4] * 16 + 0          # seq 2: position 64
+    assert s[3] == pages[3][6] * 16 + 4          # seq 3: position 100
+    assert s[4:].tolist() == [pages[4][t // 16] * 16 + t % 16 for t in range(48)]
+    assert out["kv_indices"].tolist() == sum((pages[i][:n].tolist() for i, n in enumerate([2, 3, 5, 7, 3])), [])
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("ps", [1, 16, 64])
+def test_index_c_oracle_vs_python(seed, ps):
+    rng = np.random.default_rng(seed)
+    B = int(rng.integers(1, 40))
+    prior = rng.integers(0, 300, B).astype(np.int32)
+    fresh = rng.integers(0, 70, B).astype(np.int32)
+    prior[rng.random(B) < 0.2] = 0
+    fresh[rng.random(B) < 0.2] = 0
+    W = int(-(-(prior + fresh).max() // ps)) + 2
+    R = B + 5
+    pt = rng.permutation(R * W * 2)[: R * W].astype(np.int32).reshape(R, W)
+    tix = rng.permutation(R)[:B].astype(np.int32)
+    got = orc.build_index(prior, fresh, pt, ps, table_index=tix)
+    want = orc.py_build_index(prior, fresh, pt, ps, table_index=tix)
+    assert got["err"] == 0
+    for name in want:
+        assert np.array_equal(got[name], want[name]), name
+
+
+def test_index_oracle_error_bits():
+    pt = np.array([[5, 6], [7, 8]], np.int32)
+    # row too short: 3 pages needed, 2 available
+    out = orc.build_index([30], [10], pt, 16, max_pages_per_row=2)
+    assert out["err"] & orc.ROW_OVERFLOW
+    # page id outside the pool
+    out = orc.build_index([0], [3], pt, 16, num_pages=6)
+    assert out["err"] == 0
+    out = orc.build_index([0, 0], [3, 3], pt, 16, num_pages=6)
+    assert out["err"] & orc.PAGE_RANGE and out["slot_mapping"][3:].tolist() == [-1, -1, -1]
+    # bad table row
+    out = orc.build_index([0], [3], pt, 16, table_index=[9])
+    assert out["err"] & orc.TABLE_ROW and out["slot_mapping"].tolist() == [-1, -1, -1]
+    assert out["kv_indptr"].tolist() == [0, 0]
+    # negative lengths count as zero
+    out = orc.build_index([-4], [2], pt, 16)
+    assert out["err"] & orc.NEGATIVE_LEN and out["slot_mapping"].tolist() == [5 * 16, 5 * 16 + 1]
+    # capacities
+    out = orc.build_index([0, 0], [20, 20], pt, 16, kv_indices_capacity=3, slot_capacity=30)
+    assert out["err"] & orc.INDICES_CAP and out["err"] & orc.SLOTS_CAP
+
+
+def test_index_oracle_empty_batch():
+    out = orc.build_index(np.zeros(0, np.int32), np.zeros(0, np.int32), np.zeros((1, 4), np.int32), 16)
+    assert out["kv_indptr"].tolist() == [0] and out["qo_indptr"].tolist() == [0]
+    assert out["kv_indices"].size == 0 and out["slot_mapping"].size == 0 and out["err"] == 0
+
+
+# --- store: behaviours pinned by test/mha_kvcache_test.cpp -----------------
+def _rand_rows(rng, shape, dtype=np.float32):
+    return rng.standard_normal(shape).astype(dtype)
+
+
+def test_store_places_rows():  # TestStoreKVStoresCorrectly (mha_kvcache_test.cpp:260-333)
+    rng = np.random.default_rng(0)
+    H, D, P = 8, 64, 8
+    k = _rand_rows(rng, (6, H * D))
+    v = _rand_rows(rng, (6, H * D))
+    loc = rng.permutation(6).astype(np.int64)
+    kc = np.zeros((P, H * D), np.float32)
+    vc = np.zeros_like(kc)
+    copied, err = orc.store(k, v, kc, vc, loc)
+    assert copied == 12 and err == 0
+    for i, s in enumerate(loc):
+        assert np.array_equal(kc[s], k[i]) and np.array_equal(vc[s], v[i])
+    assert not kc[6:].any()
+
+
+def test_store_second_write_wins():  # TestStoreKVOverwritesSamePage (:338-393)
+    rng = np.random.default_rng(1)
+    kc = np.zeros((8, 512), np.float32)
+    vc = np.zeros_like(kc)
+    loc = np.array([1], np.int64)
+    k1, v1, k2, v2 = (_rand_rows(rng, (1, 512)) for _ in range(4))
+    orc.store(k1, v1, kc, vc, loc)
+    orc.store(k2, v2, kc, vc, loc)
+    assert np.array_equal(kc[1], k2[0]) and np.array_equal(vc[1], v2[0])
+
+
+def test_store_empty_is_noop():  # TestStoreKVWithEmptyInput (:398-435)
+    kc = np.ones((8, 512), np.float32)
+    vc = np.ones_like(kc)
+    e = np.zeros((0, 512), np.float32)
+    assert orc.store(e, e, kc, vc, np.zeros(0, np.int64)) == (0, 0)
+    assert (kc == 1).all() and (vc == 1).all()
+
+
+def test_store_random_writes_last_writer():  # TestStoreKVMultipleRandomWrites (:473-575), seeded
+    rng = np.random.default_rng(3)
+    P, E = 128, 512
+    kc = np.zeros((P, E), np.float32)
+    vc = np.zeros_like(kc)
+    last = {}
+    for _ in range(500):
+        n = int(rng.integers(1, 13))
+        loc = rng.permutation(P)[:n].astype(np.int64)
+        k = _rand_rows(rng, (n, E))
+        v = _rand_rows(rng, (n, E))
+        orc.store(k, v, kc, vc, loc)
+        for i, s in enumerate(loc):
+            last[int(s)] = (k[i].copy(), v[i].copy())
+    for s, (kk, vv) in last.items():
+        assert np.array_equal(kc[s], kk) and np.array_equal(vc[s], vv)
+
+
+@pytest.mark.parametrize("threads", [1, 4])
+def test_store_c_vs_python_multilayer(threads):
+    rng = np.random.default_rng(4)
+    L, N, S, E = 3, 37, 200, 96
+    k = rng.integers(0, 2**16, (L, N, E), dtype=np.uint16)
+    v = rng.integers(0, 2**16, (L, N, E), dtype=np.uint16)
+    slots = rng.permutation(S)[:N].astype(np.int32)
+    slots[5] = -1  # padding token
+    kc = rng.integers(0, 2**16, (L, S, E), dtype=np.uint16)
+    vc = kc.copy() ^ 0x5A5A
+    kc2, vc2 = kc.copy(), vc.copy()
+    copied, err = orc.store(k, v, kc, vc, slots, num_slots=S, threads=threads)
+    orc.py_store(k, v, kc2, vc2, slots)
+    assert err == 0 and copied == 2 * L * (N - 1)
+    assert np.array_equal(kc, kc2) and np.array_equal(vc, vc2)
+
+
+def test_store_slot_range_error():
+    kc = np.zeros((4, 64), np.uint8)
+    vc = np.zeros_like(kc)
+    k = np.ones((2, 64), np.uint8)
+    copied, err = orc.store(k, k, kc, vc, np.array([1, 7], np.int64), num_slots=4)
+    assert copied == 2 and err == orc.SLOT_RANGE and kc[1].all() and not kc[[0, 2, 3]].any()

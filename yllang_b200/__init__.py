@@ -1,0 +1,38 @@
+"""yllang_b200 — B200-native paged KV-cache store and batch index build.
+
+The hot path of one YLLang serving step, rebuilt for sm_100a:
+
+* ``store_kv_cache`` / the C ABI ``yl_kv_store``: scatter the step's new K/V
+  rows into the layer-major paged pool by slot mapping (YLLang's
+  StoreKVCache / MHAKVCache::StoreKV);
+* ``build_index`` / ``yl_build_index``: the batch's kv_indptr, kv_indices,
+  kv_last_page_len, qo_indptr and slot_mapping (the index work of YLLang's
+  BatchManager::NextBatch), in the paged-KV format flashinfer consumes.
+
+The kernels live in libyl_kvpath.so (built in-tree); the C++ libtorch front
+end with YLLang's class names (MHAKVCache, KVCacheManager, BatchManager,
+StoreKVCache) is the extension ``yllang_b200._C`` (``load_extension()``).
+"""
+from __future__ import annotations
+
+from ._abi import (DEVERR_INDICES_CAP, DEVERR_INDPTR_OVERFLOW, DEVERR_NEGATIVE_LEN, DEVERR_PAGE_RANGE,
+                   DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW, KVPathError, lib)
+from .ops import BatchIndex, PanicError, build_index, store_args, store_kv_cache
+
+__all__ = [
+    "BatchIndex", "KVPathError", "PanicError", "build_index", "store_args", "store_kv_cache", "lib",
+    "load_extension", "DEVERR_SLOT_RANGE", "DEVERR_PAGE_RANGE", "DEVERR_ROW_OVERFLOW", "DEVERR_INDICES_CAP",
+    "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW",
+]
+
+_ext = None
+
+
+def load_extension():
+    """Import the C++ libtorch front end (building it in-tree if needed)."""
+    global _ext
+    if _ext is None:
+        from . import _build
+        _build.build_library()
+        _ext = _build.build_extension()
+    return _ext

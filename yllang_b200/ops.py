@@ -1,0 +1,166 @@
+"""Torch-tensor front end of the C ABI, for Python callers, tests and the bench.
+
+Each function checks its tensors the way the reference's TensorMatcher does
+for StoreKVCache (src/kvcache/store_kv_cache.cu:108-124: caches [*, E] with
+stride [cs, 1], inputs [N, E] with stride [ks, 1], indices [N] with stride
+[1], one device, one dtype), turns them into the raw pointers and byte
+strides of yl_store_args / yl_index_args, and calls libyl_kvpath.so on the
+current CUDA stream.  A contract violation raises PanicError before any
+launch, as RuntimeCheck does in the reference (src/include/util/panic.h:35).
+"""
+from __future__ import annotations
+
+from typing import NamedTuple
+
+import torch
+
+from . import _abi
+
+
+class PanicError(RuntimeError):
+    """Contract violation detected on the host (yllang::PanicError)."""
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise PanicError(msg)
+
+
+def _stream(stream: torch.cuda.Stream | None, device: torch.device) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return s.cuda_stream
+
+
+def store_args(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+               slots: torch.Tensor, error_word: torch.Tensor | None = None,
+               check_slots: bool = True) -> _abi.StoreArgs:
+    """Validate and pack one store call.
+
+    Per-layer form (the reference's): k, v [N, E]; k_cache, v_cache [S, E].
+    All-layers form: k, v [L, N, E]; k_cache, v_cache [L, S, E].
+    """
+    _check(k.dim() in (2, 3), f"k must be [N, E] or [L, N, E], got {tuple(k.shape)}")
+    multi = k.dim() == 3
+    for name, t in (("v", v), ("k_cache", k_cache), ("v_cache", v_cache)):
+        _check(t.dim() == k.dim(), f"{name} rank {t.dim()} != k rank {k.dim()}")
+    _check(k.shape == v.shape, f"v shape {tuple(v.shape)} != k shape {tuple(k.shape)}")
+    _check(k_cache.shape == v_cache.shape, "k_cache and v_cache shapes differ")
+    _check(k_cache.stride() == v_cache.stride(), "k_cache and v_cache strides differ")
+    E = k.shape[-1]
+    _check(k_cache.shape[-1] == E, f"cache row {k_cache.shape[-1]} != input row {E}")
+    if multi:
+        _check(k_cache.shape[0] == k.shape[0], "layer counts of inputs and caches differ")
+    for name, t in (("k", k), ("v", v), ("k_cache", k_cache), ("v_cache", v_cache)):
+        _check(t.stride(-1) == 1, f"{name} rows must be contiguous (stride[-1] == 1)")
+        _check(t.dtype == k.dtype, f"{name} dtype {t.dtype} != {k.dtype}")
+        _check(t.device == k.device, f"{name} on {t.device}, expected {k.device}")
+    _check(k.is_cuda, "tensors must be CUDA tensors")
+    N = k.shape[-2]
+    _check(slots.dim() == 1 and slots.shape[0] == N, f"slots must be [N={N}], got {tuple(slots.shape)}")
+    _check(slots.stride(0) == 1 or N <= 1, "slots must be contiguous")
+    _check(slots.dtype in (torch.int32, torch.int64), f"slots dtype {slots.dtype} must be int32 or int64")
+    _check(slots.device == k.device, "slots on another device")
+    item = k.element_size()
+    a = _abi.StoreArgs()
+    a.k, a.v = k.data_ptr(), v.data_ptr()
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.slots = slots.data_ptr()
+    a.slot_is_int64 = int(slots.dtype == torch.int64)
+    a.num_layers = k.shape[0] if multi else 1
+    a.num_tokens = N
+    a.row_bytes = E * item
+    a.k_row_stride = k.stride(-2) * item
+    a.v_row_stride = v.stride(-2) * item
+    a.cache_row_stride = k_cache.stride(-2) * item
+    if multi:
+        a.k_layer_stride = k.stride(0) * item
+        a.v_layer_stride = v.stride(0) * item
+        a.cache_layer_stride = k_cache.stride(0) * item
+    a.num_slots = k_cache.shape[-2] if check_slots else 0
+    a.error_word = error_word.data_ptr() if error_word is not None else None
+    return a
+
+
+def store_kv_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                   slots: torch.Tensor, error_word: torch.Tensor | None = None,
+                   stream: torch.cuda.Stream | None = None) -> None:
+    """k_cache[..., slots[i], :] = k[..., i, :] (and v), asynchronously.
+
+    Mirrors yllang::StoreKVCache (src/kvcache/store_kv_cache.cu:95-163) with
+    the row size taken at run time; a [L, N, E] input stores all L layers in
+    one launch.
+    """
+    if k.shape[-2] == 0:
+        return
+    args = store_args(k, v, k_cache, v_cache, slots, error_word)
+    _abi.check(_abi.kv_store_raw(args, _stream(stream, k.device)))
+
+
+class BatchIndex(NamedTuple):
+    """Page arrays of one batch, in the paged-KV format of flashinfer."""
+
+    kv_indptr: torch.Tensor
+    kv_indices: torch.Tensor
+    kv_last_page_len: torch.Tensor
+    qo_indptr: torch.Tensor
+    slot_mapping: torch.Tensor
+
+
+def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torch.Tensor, page_size: int,
+                table_index: torch.Tensor | None = None, num_pages: int = 0, kv_indices_capacity: int | None = None,
+                slot_capacity: int | None = None, slot_dtype: torch.dtype = torch.int64,
+                error_word: torch.Tensor | None = None, out: BatchIndex | None = None,
+                stream: torch.cuda.Stream | None = None) -> BatchIndex:
+    """Build kv_indptr / kv_indices / kv_last_page_len / qo_indptr / slot_mapping.
+
+    prior_len, new_len: int32 [B] on the device.  page_table: int32 [R, W]
+    with unit column stride.  The capacities bound the two ragged outputs;
+    when omitted they are computed from the lengths, which costs a device to
+    host read (pass them, or `out`, on a hot path).
+    """
+    dev = prior_len.device
+    _check(prior_len.is_cuda, "prior_len must be a CUDA tensor")
+    for name, t in (("prior_len", prior_len), ("new_len", new_len), ("page_table", page_table)):
+        _check(t.dtype == torch.int32, f"{name} must be int32, got {t.dtype}")
+        _check(t.device == dev, f"{name} on {t.device}, expected {dev}")
+    B = prior_len.shape[0]
+    _check(prior_len.dim() == 1 and new_len.shape == (B,), "prior_len and new_len must both be [B]")
+    _check(prior_len.is_contiguous() and new_len.is_contiguous(), "lengths must be contiguous")
+    _check(page_table.dim() == 2 and page_table.stride(1) == 1, "page_table must be [R, W] with unit column stride")
+    if table_index is not None:
+        _check(table_index.dtype == torch.int32 and table_index.shape == (B,) and table_index.is_contiguous(),
+               "table_index must be contiguous int32 [B]")
+    else:
+        _check(page_table.shape[0] >= B, f"page_table has {page_table.shape[0]} rows for a batch of {B}")
+    _check(slot_dtype in (torch.int32, torch.int64), "slot_dtype must be int32 or int64")
+    W = page_table.shape[1]
+    if out is None:
+        if kv_indices_capacity is None or slot_capacity is None:
+            tot = prior_len.clamp(min=0).to(torch.int64) + new_len.clamp(min=0).to(torch.int64)
+            if kv_indices_capacity is None:
+                kv_indices_capacity = int(torch.clamp((tot + page_size - 1) // page_size, max=W).sum())
+            if slot_capacity is None:
+                slot_capacity = int(new_len.clamp(min=0).to(torch.int64).sum())
+        i32 = dict(dtype=torch.int32, device=dev)
+        out = BatchIndex(torch.empty(B + 1, **i32), torch.empty(kv_indices_capacity, **i32),
+                         torch.empty(B, **i32), torch.empty(B + 1, **i32),
+                         torch.empty(slot_capacity, dtype=slot_dtype, device=dev))
+    a = _abi.IndexArgs()
+    a.prior_len, a.new_len = prior_len.data_ptr(), new_len.data_ptr()
+    a.page_table = page_table.data_ptr()
+    a.table_index = table_index.data_ptr() if table_index is not None else None
+    a.page_table_stride = page_table.stride(0)
+    a.num_table_rows = page_table.shape[0]
+    a.max_pages_per_row = W
+    a.page_size = page_size
+    a.batch_size = B
+    a.slot_is_int64 = int(out.slot_mapping.dtype == torch.int64)
+    a.num_pages = num_pages
+    a.kv_indptr, a.kv_indices = out.kv_indptr.data_ptr(), out.kv_indices.data_ptr()
+    a.kv_last_page_len, a.qo_indptr = out.kv_last_page_len.data_ptr(), out.qo_indptr.data_ptr()
+    a.slot_mapping = out.slot_mapping.data_ptr()
+    a.kv_indices_capacity = out.kv_indices.numel()
+    a.slot_capacity = out.slot_mapping.numel()
+    a.error_word = error_word.data_ptr() if error_word is not None else None
+    _abi.check(_abi.build_index_raw(a, _stream(stream, dev)))
+    return out
