@@ -211,6 +211,14 @@ class Step:
     def store(self, k_pool, v_pool, err=None):
         yl.store_kv_cache(self.k, self.v, k_pool, v_pool, self.out.slot_mapping, error_word=err)
 
+    def store_layer(self, layer, k_pool, v_pool, err=None):
+        yl.store_kv_cache(self.k[layer], self.v[layer], k_pool[layer], v_pool[layer], self.out.slot_mapping,
+                          error_word=err)
+
+    def fused(self, k_pool, v_pool, err=None):
+        yl.kv_step(self.prior, self.new, self.table, self.b.page_size, self.k, self.v, k_pool, v_pool, self.out,
+                   num_pages=self.b.num_pages, error_word=err)
+
 
 def input_bytes(b: workloads.Batch) -> int:
     """Device bytes of one rotation set's inputs (K/V rows + page table)."""
@@ -220,7 +228,7 @@ def input_bytes(b: workloads.Batch) -> int:
 def plan(args, world, free_bytes):
     """Pick the rotation count (inputs over 2.2 x L2 unless one set already is)
     and the pool size (what is left after the inputs, at most --pool-gb)."""
-    probe, _ = make_batches(args.workload, world, 1e9, 1)
+    probe, _ = make_batches(args.workload, world, 150e9, 1)  # lengths only; any pool that fits the step
     per_set = input_bytes(probe[0])
     R = args.rotate if args.rotate > 0 else max(1, min(8, math.ceil(2.2 * L2_BYTES / per_set)))
     pool_bytes = min(args.pool_gb * 1e9, free_bytes - R * per_set - 12e9)
@@ -228,19 +236,40 @@ def plan(args, world, free_bytes):
     return R, pool_bytes, per_set
 
 
-def capture(steps, order, k_pool, v_pool, err):
-    """One CUDA graph running the steps in `order`, with a timing event before,
-    between and after the two launches of every step."""
-    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)] for _ in order]
+def capture(order, launches):
+    """One CUDA graph running, for every step r in `order`, the callables
+    launches(r) in sequence.  No event nodes go inside the graph: an event
+    record between two kernels delays the second by microseconds."""
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        for j, r in enumerate(order):
-            evs[j][0].record()
-            steps[r].index(err)
-            evs[j][1].record()
-            steps[r].store(k_pool, v_pool, err)
-            evs[j][2].record()
-    return g, evs
+        for r in order:
+            for fn in launches(r):
+                fn()
+    return g
+
+
+def time_graphs(graphs, reps=1):
+    """Device time (ms) of replaying `graphs` in order, `reps` times, bracketed
+    by events on the launching stream after a synchronize."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(reps):
+        for g in graphs:
+            g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
+def per_launch_us(R, launches, n, reps=4):
+    """Mean device time (us) of one step of `launches` over n back-to-back
+    steps in a graph (replayed `reps` times after one warm-up replay)."""
+    g = capture([j % R for j in range(n)], launches)
+    g.replay()
+    us = time_graphs([g], reps) * 1e3 / (reps * n)
+    del g
+    return us
 
 
 def load_peaks():
@@ -384,27 +413,33 @@ def run_ours(args, world, rank, local):
     k_pool, v_pool = pool[0], pool[1]
     steps = [Step(b, dev, seed=1000 * rank + r) for r, b in enumerate(batches)]
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    step_bytes = b0.step_bytes()
     store_bytes = b0.store_bytes()
     index_bytes = b0.index_bytes()
-    in_bytes_per_set = per_set
-    two_launch = b0.batch > 16384
-    launches_per_step = 3 if two_launch else 2
+    fused = args.path == "fused"
+    step_mode = os.environ.get("YL_STEP_MODE", "pdl") if fused else "separate calls"
+    index_launches = 2 if b0.batch > 16384 else 1  # the two-launch index form for huge batches
+    launches_per_step = 1 if step_mode == "fused" and b0.batch <= 4096 else index_launches + 1
+
+    def step_launches(r):
+        s = steps[r]
+        if fused:
+            return [lambda: s.fused(k_pool, v_pool, err)]
+        return [lambda: s.index(err), lambda: s.store(k_pool, v_pool, err)]
 
     # warm-up: eager steps through the public API
     for w in range(args.warmup):
-        s = steps[w % R]
-        s.index(err)
-        s.store(k_pool, v_pool, err)
+        for fn in step_launches(w % R):
+            fn()
     torch.cuda.synchronize()
     assert int(err.item()) == 0, f"device error word {int(err.item()):#x} during warm-up"
 
-    # graphs: chunk of C steps replayed q times + remainder, events per launch
+    # timed steps: a graph of C steps replayed q times + a remainder graph
     K = args.steps
     C = min(K, args.chunk)
     q, rem = divmod(K, C)
-    g_main, ev_main = capture(steps, [j % R for j in range(C)], k_pool, v_pool, err)
-    g_rem, ev_rem = (capture(steps, [(q * C + j) % R for j in range(rem)], k_pool, v_pool, err)
-                     if rem else (None, []))
+    g_main = capture([j % R for j in range(C)], step_launches)
+    g_rem = capture([(q * C + j) % R for j in range(rem)], step_launches) if rem else None
     g_main.replay()  # untimed graph warm-up
     torch.cuda.synchronize()
 
@@ -423,16 +458,22 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     ms_max = reduce_max(ms, world)
-    idx_ms = [e[0].elapsed_time(e[1]) for e in ev_main + ev_rem]
-    st_ms = [e[1].elapsed_time(e[2]) for e in ev_main + ev_rem]
+    assert int(err.item()) == 0, f"device error word {int(err.item()):#x}"
+    del g_main, g_rem
+
+    # each kernel on its own, back to back in a graph: the standalone index
+    # build, the all-layer store, and the reference's one store per layer
+    n_sep = min(K, 256)
+    index_us = per_launch_us(R, lambda r: [lambda: steps[r].index(err)], n_sep)
+    store_us = per_launch_us(R, lambda r: [lambda: steps[r].store(k_pool, v_pool, err)], n_sep)
+    layer_us = per_launch_us(R, lambda r: [(lambda l: (lambda: steps[r].store_layer(l, k_pool, v_pool, err)))(
+        layer) for layer in range(L)], min(K, 16)) / L
     assert int(err.item()) == 0, f"device error word {int(err.item()):#x}"
 
     per_step_s = ms_max / 1e3 / K
     total_store = reduce_sum(float(store_bytes), world)
     value = total_store / per_step_s / 1e9
     tokens_global = b0.tokens  # every rank stores its head slice of every token
-    store_us = statistics.mean(st_ms) * 1e3
-    index_us = statistics.mean(idx_ms) * 1e3
     peak, peak_kind = load_peaks()
     achieved = store_bytes / (store_us * 1e-6) / 1e9
 
@@ -443,35 +484,41 @@ def run_ours(args, world, rank, local):
         else:
             e2e = {"value": None, "unit": "GB/s", "skipped": f"one step's inputs are {per_set / 1e9:.0f} GB"}
 
-    line = None
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
-            "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded lengths and fragmented page tables, K/V N(0,1) cast to bf16",
-            "config": dict(desc, parallelism=f"kv-head shard x{world}" if world > 1 else "single GPU",
-                           l2=f"inputs rotate over {R} sets ({R * in_bytes_per_set / 1e6:.0f} MB > 2 x L2), "
-                              "distinct destination slots per set"),
-            "tokens_per_s": round(tokens_global / per_step_s, 1),
-            "pct_hbm": round(100 * value / (peak * world), 2),
-            "store_us": round(store_us, 3), "index_build_us": round(index_us, 3),
-            "store_gbs": round(achieved, 1),
-            "index_gbs": round(index_bytes / (index_us * 1e-6) / 1e9, 1),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": args.traffic,
-                         "kernel": "store_rows_kernel", "peak_source": f"{peak_kind} hbm_gbs (copy)",
-                         "algorithmic_bytes_per_launch": store_bytes},
-            "gpu_launches": launches_per_step * K,
-            "clocks": clocks.summary(),
-        }
-        if e2e is not None:
-            line["e2e"] = e2e
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
+        "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded lengths and fragmented page tables, K/V N(0,1) cast to bf16",
+        "config": dict(desc, parallelism=f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       path=(f"yl_kv_step ({step_mode})" if fused else "build_index + store_kv_cache"),
+                       l2=f"inputs rotate over {R} sets ({R * per_set / 1e6:.0f} MB > 2 x L2), "
+                          "distinct destination slots per set"),
+        "tokens_per_s": round(tokens_global / per_step_s, 1),
+        "pct_hbm": round(100 * value / (peak * world), 2),
+        "index_build_us": round(index_us, 3),
+        "step_us": round(ms_max * 1e3 / K, 3),
+        "step_gbs": round(reduce_sum(float(step_bytes), world) / per_step_s / 1e9, 1),
+        "store_us": round(store_us, 3),
+        "store_gbs": round(achieved, 1),
+        "index_gbs": round(index_bytes / (index_us * 1e-6) / 1e9, 1),
+        "per_layer_store": {"launches_per_step": L, "us_per_launch": round(layer_us, 3),
+                            "gbs": round(store_bytes / L / (layer_us * 1e-6) / 1e9, 1)},
+        "roofline": {"bound": "hbm", "kernel": "store_rows_kernel (all layers of a step, one launch)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": args.traffic,
+                     "peak_source": f"{peak_kind} hbm_gbs (copy)", "algorithmic_bytes_per_launch": store_bytes,
+                     "launch_us": round(store_us, 3),
+                     "timing": f"{n_sep} back-to-back launches in one CUDA graph, events around the replays"},
+        "gpu_launches": K * launches_per_step,
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_store_step_sample(b0, seconds=args.cpu_seconds)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    del g_main, g_rem
+    print(json.dumps(line), flush=True)
 
 
 def run_e2e(args, steps, k_pool, v_pool, err, world):
@@ -495,9 +542,8 @@ def run_e2e(args, steps, k_pool, v_pool, err, world):
             if dk[n].shape != h[n].shape:
                 dk[n] = torch.empty(h[n].shape, dtype=h[n].dtype, device=dev)
             dk[n].copy_(h[n], non_blocking=True)
-        yl.build_index(dk["prior"], dk["new"], dk["table"], b.page_size, num_pages=b.num_pages, out=out,
-                       error_word=err)
-        yl.store_kv_cache(dk["k"], dk["v"], k_pool, v_pool, out.slot_mapping, error_word=err)
+        yl.kv_step(dk["prior"], dk["new"], dk["table"], b.page_size, dk["k"], dk["v"], k_pool, v_pool, out,
+                   num_pages=b.num_pages, error_word=err)
         err_host.copy_(err, non_blocking=True)
 
     for r in range(min(3, R)):
@@ -517,7 +563,7 @@ def run_e2e(args, steps, k_pool, v_pool, err, world):
     total = reduce_sum(float(b.store_bytes()), world)
     return {"value": round(total / per / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": 4, "steps": E, "ms_per_step": round(ms / E, 4),
-            "path": "pinned host -> device copies, yllang_b200.build_index + store_kv_cache, error word -> host"}
+            "path": "pinned host -> device copies, yllang_b200.kv_step, error word -> host"}
 
 
 def main():
@@ -527,6 +573,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="llama3_decode")
+    ap.add_argument("--path", choices=["fused", "separate"], default="fused",
+                    help="timed step: yl_kv_step, or build_index + store_kv_cache as two calls")
     ap.add_argument("--rotate", type=int, default=0, help="input sets cycled through (0: enough to exceed 2.2 x L2)")
     ap.add_argument("--chunk", type=int, default=256, help="steps per captured CUDA graph")
     ap.add_argument("--pool-gb", type=float, default=150.0)

@@ -67,6 +67,7 @@ typedef enum yl_status {
 #define YL_DEVERR_NEGATIVE_LEN    0x20u /* index: a negative length (treated as 0)          */
 #define YL_DEVERR_INDPTR_OVERFLOW 0x40u /* index: a running sum passed INT32_MAX (no fill)  */
 #define YL_DEVERR_TABLE_ROW       0x80u /* index: table_index outside [0, num_table_rows)   */
+#define YL_DEVERR_TOKEN_COUNT     0x100u /* step: sum of new_len differs from num_tokens      */
 
 /*
  * Store (replaces yllang::StoreKVCache<kElementSize>,
@@ -143,7 +144,9 @@ YL_API int yl_kv_store(const yl_store_args *args, cudaStream_t stream);
  * when num_pages > 0 (kv_indices keeps the id, the slot is written as -1),
  * table_index outside [0, num_table_rows) (the sequence gets no pages and
  * -1 slots), sum of np_i > kv_indices_capacity, sum of new_len >
- * slot_capacity, negative lengths (treated as 0).
+ * slot_capacity, negative lengths (treated as 0).  slot_mapping entries past
+ * qo_indptr[B], up to slot_capacity, are set to -1 (padding), so a store
+ * given the whole buffer skips them.
  * Any outputs except kv_indptr/qo_indptr may be NULL to skip them.
  */
 typedef struct yl_index_args {
@@ -171,6 +174,29 @@ typedef struct yl_index_args {
 } yl_index_args;
 
 YL_API int yl_build_index(const yl_index_args *args, cudaStream_t stream);
+
+/*
+ * Step: yl_build_index(&index) followed by yl_kv_store of every layer with
+ * slots = index.slot_mapping, fused into one launch when the batch has at
+ * most 4096 sequences and the rows have a 16-byte fast shape (else the two
+ * launches run back to back).  The result is identical to the two calls.
+ * This is one serving step of the reference's path: the per-step index work
+ * of BatchManager::NextBatch (src/include/batch/batch_manager.h:97-112)
+ * followed by MHAKVCache::StoreKV (src/include/kvcache/mha_kvcache.h:76-86)
+ * for every layer.
+ *
+ * index.slot_mapping is required, with slot_capacity >= store.num_tokens;
+ * store.slots, store.slot_is_int64 and store.error_word are ignored (the
+ * slots are index.slot_mapping, errors go to index.error_word).
+ * store.num_tokens must equal the sum of new_len (else
+ * YL_DEVERR_TOKEN_COUNT; tokens without a sequence are not stored).
+ */
+typedef struct yl_step_args {
+  yl_index_args index;
+  yl_store_args store;
+} yl_step_args;
+
+YL_API int yl_kv_step(const yl_step_args *args, cudaStream_t stream);
 
 /* Human-readable name of a yl_status value (static storage). */
 YL_API const char *yl_status_string(int status);

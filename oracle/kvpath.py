@@ -55,7 +55,8 @@ def build(with_reference: bool = False) -> None:
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        src = os.path.join(_HERE, "kvpath_oracle.c")
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(src) > os.path.getmtime(_LIB_PATH):
             build()
         L = ctypes.CDLL(_LIB_PATH)
         L.oracle_kv_store.restype = _i64

@@ -116,7 +116,8 @@ int64_t oracle_kv_store(const uint8_t *k, const uint8_t *v, uint8_t *k_cache, ui
 
 /*
  * Index build.  All arrays are host arrays; outputs may be NULL except
- * kv_indptr and qo_indptr.  Returns 0, or -1 when a running sum passes
+ * kv_indptr and qo_indptr.  Slot entries past the batch's new tokens, up to
+ * slot_capacity, are set to -1.  Returns 0, or -1 when a running sum passes
  * INT32_MAX (outputs other than the error word are then unspecified).
  */
 int oracle_build_index(const int32_t *prior_len, const int32_t *new_len, const int32_t *page_table,
@@ -192,6 +193,11 @@ int oracle_build_index(const int32_t *prior_len, const int32_t *new_len, const i
     }
     kv_indptr[i + 1] = (int32_t)kv_off;
     qo_indptr[i + 1] = (int32_t)qo_off;
+  }
+  /* slot entries past the batch's tokens, up to the capacity, hold -1 */
+  for (int64_t e = qo_off; rc == 0 && e < slot_capacity; ++e) {
+    if (slot_is_int64) ((int64_t *)slot_mapping)[e] = -1;
+    else ((int32_t *)slot_mapping)[e] = -1;
   }
   if (kv_off > kv_indices_capacity && kv_indices) err |= ORACLE_INDICES_CAP;
   if (qo_off > slot_capacity && slot_mapping) err |= ORACLE_SLOTS_CAP;

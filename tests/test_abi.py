@@ -47,7 +47,8 @@ def _c_layout(tmp_path, struct, fields):
     return {k: int(v) for k, v in (line.split() for line in out.strip().splitlines())}
 
 
-@pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs)])
+@pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs),
+                                        ("yl_step_args", _abi.StepArgs)])
 def test_struct_layout_matches_header(tmp_path, struct, cls):
     names = [f for f, _ in cls._fields_]
     c = _c_layout(tmp_path, struct, names)

@@ -16,23 +16,26 @@ StoreKVCache) is the extension ``yllang_b200._C`` (``load_extension()``).
 from __future__ import annotations
 
 from ._abi import (DEVERR_INDICES_CAP, DEVERR_INDPTR_OVERFLOW, DEVERR_NEGATIVE_LEN, DEVERR_PAGE_RANGE,
-                   DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW, KVPathError, lib)
-from .ops import BatchIndex, PanicError, build_index, store_args, store_kv_cache
+                   DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW, DEVERR_TOKEN_COUNT,
+                   KVPathError, lib)
+from .ops import BatchIndex, PanicError, build_index, kv_step, store_args, store_kv_cache
 
 __all__ = [
-    "BatchIndex", "KVPathError", "PanicError", "build_index", "store_args", "store_kv_cache", "lib",
+    "BatchIndex", "KVPathError", "PanicError", "build_index", "kv_step", "store_args", "store_kv_cache", "lib",
     "load_extension", "DEVERR_SLOT_RANGE", "DEVERR_PAGE_RANGE", "DEVERR_ROW_OVERFLOW", "DEVERR_INDICES_CAP",
-    "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW",
+    "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW", "DEVERR_TOKEN_COUNT",
 ]
 
 _ext = None
 
 
 def load_extension():
-    """Import the C++ libtorch front end (building it in-tree if needed)."""
+    """Import the C++ libtorch front end yllang_b200._C (built in-tree by
+    __graft_entry__.build(); a missing build is an ImportError)."""
     global _ext
     if _ext is None:
-        from . import _build
-        _build.build_library()
-        _ext = _build.build_extension()
+        import torch  # noqa: F401  (libtorch must be loaded first)
+
+        from . import _C
+        _ext = _C
     return _ext

@@ -28,6 +28,7 @@ DEVERR_SLOTS_CAP = 0x10
 DEVERR_NEGATIVE_LEN = 0x20
 DEVERR_INDPTR_OVERFLOW = 0x40
 DEVERR_TABLE_ROW = 0x80
+DEVERR_TOKEN_COUNT = 0x100
 
 ABI_VERSION = 1
 
@@ -86,8 +87,15 @@ class IndexArgs(ctypes.Structure):
     ]
 
 
+class StepArgs(ctypes.Structure):
+    """struct yl_step_args."""
+
+    _fields_ = [("index", IndexArgs), ("store", StoreArgs)]
+
+
 # Every symbol include/yl_kvpath.h declares.
-EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_status_string", "yl_last_error", "yl_abi_version")
+EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_status_string", "yl_last_error",
+                    "yl_abi_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -113,6 +121,8 @@ def lib() -> ctypes.CDLL:
         L.yl_kv_store.argtypes = [ctypes.POINTER(StoreArgs), _vp]
         L.yl_build_index.restype = ctypes.c_int
         L.yl_build_index.argtypes = [ctypes.POINTER(IndexArgs), _vp]
+        L.yl_kv_step.restype = ctypes.c_int
+        L.yl_kv_step.argtypes = [ctypes.POINTER(StepArgs), _vp]
         L.yl_status_string.restype = ctypes.c_char_p
         L.yl_status_string.argtypes = [ctypes.c_int]
         L.yl_last_error.restype = ctypes.c_char_p
@@ -144,3 +154,7 @@ def kv_store_raw(args: StoreArgs, stream: int | None) -> int:
 
 def build_index_raw(args: IndexArgs, stream: int | None) -> int:
     return lib().yl_build_index(ctypes.byref(args), stream)
+
+
+def kv_step_raw(args: StepArgs, stream: int | None) -> int:
+    return lib().yl_kv_step(ctypes.byref(args), stream)

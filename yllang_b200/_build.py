@@ -3,8 +3,8 @@
 * libyl_kvpath.so — the C-ABI CUDA library (kernels + yl_* entry points),
   compiled by nvcc for sm_100a only; depends on the CUDA runtime, not torch.
 * _C*.so — the C++17 libtorch front end (yllang::StoreKVCache, MHAKVCache,
-  the batch index builder and page allocator) as a torch extension linked
-  against libyl_kvpath.so.
+  the batch index builder and page allocator) as a Python extension linked
+  against libtorch and libyl_kvpath.so.
 
 Both land inside the package directory so that they travel with the source
 tree and are the files a process loads.
@@ -23,7 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libyl_kvpath.so")
 
-CUDA_SOURCES = ["common.cu", "kv_store.cu", "index_build.cu"]
+CUDA_SOURCES = ["common.cu", "kv_store.cu", "index_build.cu", "kv_step.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -56,24 +56,49 @@ def build_library(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
-def build_extension(force: bool = False, verbose: bool = False):
-    """Build and import the libtorch front end (yllang_b200._C)."""
+def _ext_path() -> str:
+    import sysconfig
+    return os.path.join(PKG, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_extension(force: bool = False, verbose: bool = False) -> str:
+    """g++-compile the libtorch front end into yllang_b200/_C*.so, linked
+    against libyl_kvpath.so (found next to it at run time via $ORIGIN)."""
+    import sysconfig
+
+    import torch
     from torch.utils import cpp_extension
 
+    out = _ext_path()
+    tdir = os.path.join(CSRC, "torch")
+    srcs = sorted(glob.glob(os.path.join(tdir, "*.cpp")))
+    deps = srcs + glob.glob(os.path.join(tdir, "*.h")) + [os.path.join(INCLUDE, "yl_kvpath.h")]
+    if not force and not _stale(out, deps):
+        return out
     build_dir = os.path.join(PKG, "_build")
     os.makedirs(build_dir, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "torch", "*.cpp")))
-    mod = cpp_extension.load(
-        name="yllang_b200_C",
-        sources=srcs,
-        extra_include_paths=[INCLUDE, os.path.join(CSRC, "torch")],
-        extra_cflags=["-O2", "-std=c++17"],
-        extra_ldflags=[f"-L{PKG}", "-lyl_kvpath", f"-Wl,-rpath,{PKG}"],
-        build_directory=build_dir,
-        verbose=verbose,
-        with_cuda=True,
-    )
-    return mod
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    abi = getattr(cpp_extension, "_get_pybind11_abi_build_flags", lambda: [])()
+    cflags = ["-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden",
+              f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+              "-DTORCH_EXTENSION_NAME=_C", "-DTORCH_API_INCLUDE_EXTENSION_H", *abi,
+              f"-I{INCLUDE}", f"-I{tdir}", f"-I{sysconfig.get_paths()['include']}", f"-I{cuda_home}/include"]
+    cflags += [f"-I{p}" for p in cpp_extension.include_paths()]
+    objs, procs = [], []
+    for src in srcs:
+        obj = os.path.join(build_dir, os.path.basename(src) + ".o")
+        objs.append(obj)
+        procs.append(subprocess.Popen(["g++", *cflags, "-c", src, "-o", obj]))
+    if any(p.wait() != 0 for p in procs):
+        raise RuntimeError("compiling the libtorch front end failed")
+    build_library()
+    tmp = out + ".tmp"
+    subprocess.run(["g++", "-shared", *objs, "-o", tmp, f"-L{torch_lib}", "-lc10", "-ltorch", "-ltorch_cpu",
+                    "-ltorch_python", "-lc10_cuda", "-ltorch_cuda", f"-L{PKG}", "-lyl_kvpath",
+                    "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"], check=True)
+    os.replace(tmp, out)
+    return out
 
 
 def build_all(force: bool = False, verbose: bool = False) -> None:

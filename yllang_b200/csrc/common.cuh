@@ -69,6 +69,15 @@ struct FastDiv {
   }
 };
 
+// Programmatic dependent launch.  A kernel launched with the
+// programmatic-stream-serialization attribute may start while the kernel
+// before it in the stream is still running: pdl_wait() blocks the calling
+// thread until that kernel has completed and its writes are visible (it
+// returns at once for a normal launch), and pdl_trigger() lets the next such
+// kernel start launching early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ void raise_deverr(uint32_t *word, uint32_t bit) {
   if (word != nullptr) atomicOr(word, bit);
 }

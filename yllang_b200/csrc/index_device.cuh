@@ -1,0 +1,295 @@
+// Device side of the batch index build shared by the index kernels
+// (index_build.cu) and the fused step kernel (kv_step.cu).
+//
+// The per-sequence page and token counts are exclusive-scanned into
+// kv_indptr / qo_indptr offsets (in shared memory, or in the outputs for very
+// large batches); every other output element then finds its sequence by a
+// binary search over those offsets and gathers from that sequence's
+// page-table row.
+#pragma once
+
+#include <climits>
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace ylk {
+
+struct IndexParams {
+  const int32_t *prior_len;
+  const int32_t *new_len;
+  const int32_t *page_table;
+  const int32_t *table_index;
+  int64_t page_table_stride;
+  int64_t num_pages;
+  int64_t indices_cap;
+  int64_t slots_cap;
+  int32_t *kv_indptr;
+  int32_t *kv_indices;
+  int32_t *last_page_len;
+  int32_t *qo_indptr;
+  void *slot_mapping;
+  uint32_t *error_word;
+  int32_t num_table_rows;
+  int32_t max_pages_per_row;
+  int32_t page_size;
+  int32_t batch;
+  int32_t slot64;
+  FastDiv by_page;
+};
+
+struct SeqFacts {
+  int32_t prior;  // clamped to >= 0
+  int32_t fresh;  // new tokens, clamped to >= 0
+  int32_t pages;  // np_i after validation and clamping
+  int32_t row;    // page-table row
+};
+
+// Validated per-sequence facts.  Only `report` threads raise error bits so a
+// bad input is not reported once per block.
+__device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool report) {
+  SeqFacts f;
+  int32_t pl = p.prior_len[i];
+  int32_t nl = p.new_len[i];
+  if (pl < 0 || nl < 0) {
+    if (report) raise_deverr(p.error_word, YL_DEVERR_NEGATIVE_LEN);
+    pl = max(pl, 0);
+    nl = max(nl, 0);
+  }
+  f.prior = pl;
+  f.fresh = nl;
+  f.row = i;
+  bool row_ok = true;
+  if (p.table_index != nullptr) {
+    f.row = p.table_index[i];
+    if (f.row < 0 || f.row >= p.num_table_rows) {
+      if (report) raise_deverr(p.error_word, YL_DEVERR_TABLE_ROW);
+      row_ok = false;
+    }
+  }
+  const int64_t total = static_cast<int64_t>(pl) + nl;
+  int64_t np = 0;
+  if (row_ok) {
+    const int64_t up = total + p.page_size - 1;
+    np = up < (1ll << 31) ? static_cast<int64_t>(p.by_page.div(static_cast<uint32_t>(up))) : up / p.page_size;
+  }
+  if (np > p.max_pages_per_row) {
+    if (report) raise_deverr(p.error_word, YL_DEVERR_ROW_OVERFLOW);
+    np = p.max_pages_per_row;
+  }
+  f.pages = static_cast<int32_t>(np);
+  return f;
+}
+
+// Exclusive block scan of two int64 values per thread.  `scratch` holds 64
+// int64; returns the block totals through ta/tb.  Ends synchronised.
+__device__ __forceinline__ void block_scan2(int64_t &a, int64_t &b, int64_t &ta, int64_t &tb, int64_t *scratch) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int64_t a0 = a, b0 = b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t xa = __shfl_up_sync(0xffffffffu, a, o);
+    const int64_t xb = __shfl_up_sync(0xffffffffu, b, o);
+    if (lane >= o) {
+      a += xa;
+      b += xb;
+    }
+  }
+  if (lane == 31) {
+    scratch[warp] = a;
+    scratch[32 + warp] = b;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int64_t x = lane < nwarps ? scratch[lane] : 0;
+    int64_t y = lane < nwarps ? scratch[32 + lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t xx = __shfl_up_sync(0xffffffffu, x, o);
+      const int64_t yy = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) {
+        x += xx;
+        y += yy;
+      }
+    }
+    scratch[lane] = x;
+    scratch[32 + lane] = y;
+  }
+  __syncthreads();
+  const int64_t pa = warp > 0 ? scratch[warp - 1] : 0;
+  const int64_t pb = warp > 0 ? scratch[32 + warp - 1] : 0;
+  ta = scratch[nwarps - 1];
+  tb = scratch[32 + nwarps - 1];
+  a = pa + a - a0;
+  b = pb + b - b0;
+  __syncthreads();
+}
+
+// Phase A: scan page and token counts of all sequences into kvp[0..B] and
+// qop[0..B] (shared or global memory).  The counts are first staged in
+// kvp/qop (coalesced), then every thread scans a contiguous chunk of them
+// serially and one block scan of the chunk totals gives the chunk offsets.
+// Returns false (uniformly across the block) when a sum passes INT32_MAX; the
+// fill must then be skipped.
+__device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *qop, int64_t *scratch, bool report) {
+  const int B = p.batch;
+  for (int i = threadIdx.x; i < B; i += blockDim.x) {
+    const SeqFacts f = seq_facts(p, i, report);
+    kvp[i] = f.pages;
+    qop[i] = f.fresh;
+  }
+  __syncthreads();
+  const int per = (B + blockDim.x - 1) / blockDim.x;
+  const int lo = min(B, static_cast<int>(threadIdx.x) * per);
+  const int hi = min(B, lo + per);
+  int64_t a = 0, b = 0;
+  for (int i = lo; i < hi; ++i) {
+    a += kvp[i];
+    b += qop[i];
+  }
+  int64_t ta, tb;
+  block_scan2(a, b, ta, tb, scratch);  // ends synchronised: every count has been read
+  if (ta > INT_MAX || tb > INT_MAX) {
+    if (report && threadIdx.x == 0) raise_deverr(p.error_word, YL_DEVERR_INDPTR_OVERFLOW);
+    return false;
+  }
+  for (int i = lo; i < hi; ++i) {
+    const int32_t x = kvp[i], y = qop[i];
+    kvp[i] = static_cast<int32_t>(a);
+    qop[i] = static_cast<int32_t>(b);
+    a += x;
+    b += y;
+  }
+  if (threadIdx.x == 0) {
+    kvp[B] = static_cast<int32_t>(ta);
+    qop[B] = static_cast<int32_t>(tb);
+  }
+  __syncthreads();
+  return true;
+}
+
+// Largest i in [0, n) with off[i] <= e, given off[0] <= e < off[n].
+__device__ __forceinline__ int find_seq(const int32_t *off, int n, int64_t e) {
+  int lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (off[mid] <= e) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void write_slot(const IndexParams &p, int64_t t, int64_t slot) {
+  if (p.slot64) static_cast<int64_t *>(p.slot_mapping)[t] = slot;
+  else static_cast<int32_t *>(p.slot_mapping)[t] = static_cast<int32_t>(slot);
+}
+
+// kv_indices[e] for one element e < kv_indptr[B].
+__device__ __forceinline__ void kv_index_elem(const IndexParams &p, const int32_t *kvp, int64_t e) {
+  const int i = find_seq(kvp, p.batch, e);
+  const int64_t col = e - kvp[i];
+  const int32_t row = p.table_index ? p.table_index[i] : i;
+  const int32_t page = p.page_table[static_cast<int64_t>(row) * p.page_table_stride + col];
+  if (p.num_pages > 0 && (page < 0 || page >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
+  p.kv_indices[e] = page;
+}
+
+// Slot of new token t < qo_indptr[B], or -1 when it has none (its position
+// is past the sequence's page-table row, or its page is not a pool page).
+__device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
+                                              int64_t t) {
+  const int i = find_seq(qop, p.batch, t);
+  const int64_t pos = static_cast<int64_t>(max(p.prior_len[i], 0)) + (t - qop[i]);
+  const int32_t pages = kvp[i + 1] - kvp[i];
+  if (pos >= (1ll << 31)) return -1;
+  const uint32_t pidx = p.by_page.div(static_cast<uint32_t>(pos));
+  if (static_cast<int64_t>(pidx) >= pages) return -1;
+  const int32_t row = p.table_index ? p.table_index[i] : i;
+  const int32_t page = p.page_table[static_cast<int64_t>(row) * p.page_table_stride + pidx];
+  const bool in_range = page >= 0 && (p.num_pages <= 0 || page < p.num_pages);
+  const int64_t s = static_cast<int64_t>(page) * p.page_size + (pos - static_cast<int64_t>(pidx) * p.page_size);
+  if (in_range && (p.slot64 || s <= INT_MAX)) return s;
+  raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
+  return -1;
+}
+
+// Phase C for the elements [begin, end) of [kv_indices | slot_mapping].  Slot
+// entries past qo_indptr[B] (up to the slot capacity) are written as -1.
+// Each element belongs to exactly one block, so every block reports its own.
+__device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, const int32_t *qop, int64_t n_idx,
+                           int64_t begin, int64_t end) {
+  const int64_t n_tok = qop[p.batch];
+  for (int64_t e = begin + threadIdx.x; e < end; e += blockDim.x) {
+    if (e < n_idx) {
+      kv_index_elem(p, kvp, e);
+    } else {
+      const int64_t t = e - n_idx;
+      write_slot(p, t, t < n_tok ? token_slot(p, kvp, qop, t) : -1);
+    }
+  }
+}
+
+// Phase B: per-sequence outputs for i in [first, B], stepping by `step`.
+__device__ inline void write_seq_outputs(const IndexParams &p, const int32_t *kvp, const int32_t *qop, int64_t first,
+                                  int64_t step, bool to_global_indptr) {
+  for (int64_t i = first; i <= p.batch; i += step) {
+    if (to_global_indptr) {
+      p.kv_indptr[i] = kvp[i];
+      p.qo_indptr[i] = qop[i];
+    }
+    if (i < p.batch && p.last_page_len != nullptr) {
+      const int32_t pages = kvp[i + 1] - kvp[i];
+      const int64_t total = static_cast<int64_t>(max(p.prior_len[i], 0)) + max(p.new_len[i], 0);
+      p.last_page_len[i] = pages == 0 ? 0 : static_cast<int32_t>((total - 1) % p.page_size + 1);
+    }
+  }
+}
+
+// Split of the fill space [kv_indices | slot_mapping] among blocks, with the
+// capacity checks.
+__device__ __forceinline__ void fill_block_share(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
+                                                 bool report) {
+  int64_t n_idx = p.kv_indices ? kvp[p.batch] : 0;
+  const int64_t n_slot = p.slot_mapping ? p.slots_cap : 0;
+  if (n_idx > p.indices_cap) {
+    if (report && threadIdx.x == 0) raise_deverr(p.error_word, YL_DEVERR_INDICES_CAP);
+    n_idx = p.indices_cap;
+  }
+  if (p.slot_mapping && qop[p.batch] > p.slots_cap && report && threadIdx.x == 0)
+    raise_deverr(p.error_word, YL_DEVERR_SLOTS_CAP);
+  const int64_t work = n_idx + n_slot;
+  const int64_t chunk = (work + gridDim.x - 1) / gridDim.x;
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * chunk;
+  const int64_t end = min(begin + chunk, work);
+  if (begin < end) fill_range(p, kvp, qop, n_idx, begin, end);
+}
+
+// kv_indices share of this block when the slots of tokens [0, slot_begin) are
+// written elsewhere (the fused step kernel writes them while it stores); the
+// slot entries [slot_begin, slot capacity) are set to -1 here.
+__device__ __forceinline__ void fill_kv_share(const IndexParams &p, const int32_t *kvp, int64_t slot_begin,
+                                              bool report) {
+  int64_t n_idx = p.kv_indices ? kvp[p.batch] : 0;
+  if (n_idx > p.indices_cap) {
+    if (report && threadIdx.x == 0) raise_deverr(p.error_word, YL_DEVERR_INDICES_CAP);
+    n_idx = p.indices_cap;
+  }
+  const int64_t tail = p.slot_mapping && p.slots_cap > slot_begin ? p.slots_cap - slot_begin : 0;
+  const int64_t work = n_idx + tail;
+  const int64_t chunk = (work + gridDim.x - 1) / gridDim.x;
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * chunk;
+  const int64_t end = min(begin + chunk, work);
+  for (int64_t e = begin + threadIdx.x; e < end; e += blockDim.x) {
+    if (e < n_idx) kv_index_elem(p, kvp, e);
+    else write_slot(p, slot_begin + (e - n_idx), -1);
+  }
+}
+
+// Host halves of yl_build_index (index_build.cu), shared with the fused step:
+// prepare_index validates the arguments and fills the kernel parameters,
+// launch_index launches the index kernels.
+int prepare_index(const yl_index_args *a, IndexParams &p);
+int launch_index(const IndexParams &p, cudaStream_t stream);
+
+}  // namespace ylk

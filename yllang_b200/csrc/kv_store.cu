@@ -21,102 +21,16 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
+#include "store_device.cuh"
 
 namespace ylk {
-
-struct StoreParams {
-  const char *k;
-  const char *v;
-  char *k_cache;
-  char *v_cache;
-  const void *slots;
-  int64_t k_row_stride;
-  int64_t v_row_stride;
-  int64_t cache_row_stride;
-  int64_t k_layer_stride;
-  int64_t v_layer_stride;
-  int64_t cache_layer_stride;
-  int64_t num_slots;
-  uint32_t *error_word;
-  uint32_t total_rows;  // 2 * L * N  (< 2^31)
-  uint32_t row_units;   // row_bytes / unit, generic kernel only
-  FastDiv by_tokens;    // divides a row id by N
-};
-
-// ---------------------------------------------------------------------------
-// Vector types and cache-hinted global accesses.  Loads of the step's input
-// rows are read exactly once: non-coherent path, no L1 allocation.
-// ---------------------------------------------------------------------------
-template <int W>
-struct Vec;
-template <>
-struct Vec<16> {
-  uint32_t r[4];
-};
-template <>
-struct Vec<32> {
-  uint32_t r[8];
-};
-
-__device__ __forceinline__ void load_vec(Vec<16> &x, const char *p) {
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(x.r[0]), "=r"(x.r[1]), "=r"(x.r[2]), "=r"(x.r[3])
-               : "l"(p));
-}
-__device__ __forceinline__ void store_vec(char *p, const Vec<16> &x) {
-  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(x.r[0]), "r"(x.r[1]), "r"(x.r[2]),
-               "r"(x.r[3])
-               : "memory");
-}
-__device__ __forceinline__ void load_vec(Vec<32> &x, const char *p) {
-  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(x.r[0]), "=r"(x.r[1]), "=r"(x.r[2]), "=r"(x.r[3]), "=r"(x.r[4]), "=r"(x.r[5]),
-                 "=r"(x.r[6]), "=r"(x.r[7])
-               : "l"(p));
-}
-__device__ __forceinline__ void store_vec(char *p, const Vec<32> &x) {
-  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(x.r[0]), "r"(x.r[1]),
-               "r"(x.r[2]), "r"(x.r[3]), "r"(x.r[4]), "r"(x.r[5]), "r"(x.r[6]), "r"(x.r[7])
-               : "memory");
-}
-
-template <typename SlotT>
-__device__ __forceinline__ int64_t load_slot(const void *slots, uint32_t token) {
-  return static_cast<int64_t>(__ldg(static_cast<const SlotT *>(slots) + token));
-}
-
-// True when the slot names a pool row; -1 (padding) is skipped silently and
-// anything else out of range is skipped and reported.
-__device__ __forceinline__ bool slot_ok(int64_t slot, const StoreParams &p) {
-  if (slot >= 0 && (p.num_slots <= 0 || slot < p.num_slots)) return true;
-  if (slot != -1) raise_deverr(p.error_word, YL_DEVERR_SLOT_RANGE);
-  return false;
-}
-
-struct RowAddr {
-  const char *src;
-  char *dst_base;  // pool base of this plane's layer; slot offset added later
-};
-
-__device__ __forceinline__ RowAddr row_addr(const StoreParams &p, uint32_t row, uint32_t &token) {
-  const uint32_t plane = p.by_tokens.div(row);
-  token = row - plane * p.by_tokens.d;
-  const uint32_t layer = plane >> 1;
-  RowAddr a;
-  if (plane & 1u) {
-    a.src = p.v + static_cast<int64_t>(layer) * p.v_layer_stride + static_cast<int64_t>(token) * p.v_row_stride;
-    a.dst_base = p.v_cache + static_cast<int64_t>(layer) * p.cache_layer_stride;
-  } else {
-    a.src = p.k + static_cast<int64_t>(layer) * p.k_layer_stride + static_cast<int64_t>(token) * p.k_row_stride;
-    a.dst_base = p.k_cache + static_cast<int64_t>(layer) * p.cache_layer_stride;
-  }
-  return a;
-}
 
 // Fast path: row = G lanes x VPL vectors x W bytes, R rows per group-iteration.
 template <int W, int G, int VPL, int R, typename SlotT>
@@ -125,39 +39,21 @@ __global__ void __launch_bounds__(256) store_rows_kernel(const __grid_constant__
   const uint32_t group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
   const uint32_t num_groups = (gridDim.x * blockDim.x) / G;
 
-  for (uint32_t base = group * R; base < p.total_rows; base += num_groups * R) {
-    Vec<W> data[R][VPL];
-    char *dst[R];
+  uint32_t base = group * R;
+  RowBatch<W, G, VPL, R> b;
+  b.load(p, base, lane);
+  // The K/V rows are in flight; the slots may be written by the kernel just
+  // before this one (the index build, when launched as its PDL dependent).
+  pdl_wait();
+  while (base < p.total_rows) {
     int64_t slot[R];
-    bool live[R];
-    // Issue every slot and row load of this iteration before consuming any.
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const uint32_t row = base + r;
-      live[r] = row < p.total_rows;
-      if (live[r]) {
-        uint32_t token;
-        const RowAddr a = row_addr(p, row, token);
-        slot[r] = load_slot<SlotT>(p.slots, token);
-        dst[r] = a.dst_base;
+    for (int r = 0; r < R; ++r) slot[r] = b.live[r] ? load_slot<SlotT>(p.slots, b.token[r]) : -1;
 #pragma unroll
-        for (int j = 0; j < VPL; ++j) load_vec(data[r][j], a.src + (j * G + lane) * W);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (live[r]) {
-        live[r] = slot_ok(slot[r], p);
-        dst[r] += slot[r] * p.cache_row_stride;
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (live[r]) {
-#pragma unroll
-        for (int j = 0; j < VPL; ++j) store_vec(dst[r] + (j * G + lane) * W, data[r][j]);
-      }
-    }
+    for (int r = 0; r < R; ++r) b.resolve(p, r, slot[r]);
+    b.store(lane);
+    base += num_groups * R;
+    if (base < p.total_rows) b.load(p, base, lane);
   }
 }
 
@@ -168,6 +64,7 @@ __global__ void __launch_bounds__(256) store_rows_generic_kernel(const __grid_co
   const uint32_t lane = threadIdx.x % 32;
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const uint32_t num_warps = (gridDim.x * blockDim.x) / 32;
+  pdl_wait();
   for (uint32_t row = warp; row < p.total_rows; row += num_warps) {
     uint32_t token;
     const RowAddr a = row_addr(p, row, token);
@@ -192,26 +89,18 @@ __global__ void __launch_bounds__(256) store_rows_generic_kernel(const __grid_co
 }
 
 // ---------------------------------------------------------------------------
-// Host side: pick a kernel for (row bytes, vector width, slot type), size the
-// grid to the resident capacity of the device, launch.
+// Host side: validate, pick a kernel for (row bytes, vector width, slot type),
+// size the grid to the resident capacity of the device, launch.
 // ---------------------------------------------------------------------------
 using StoreKernel = void (*)(StoreParams);
 
 struct StoreVariant {
   StoreKernel fn;
-  int group;       // lanes per row
-  int rows;        // rows per group-iteration
+  int group;  // lanes per row
+  int rows;   // rows per group-iteration
 };
 
-template <int W, int G, int VPL, int R>
-StoreVariant make_variant(bool slot64) {
-  return StoreVariant{slot64 ? store_rows_kernel<W, G, VPL, R, int64_t> : store_rows_kernel<W, G, VPL, R, int32_t>,
-                      G, R};
-}
-
-// Vector width of the fast path: 16-byte vectors by default, 32-byte (v8)
-// vectors when YL_STORE_VECTOR_BYTES=32 is set in the environment.
-static int fast_vector_bytes() {
+int fast_vector_bytes() {
   static int w = [] {
     const char *e = std::getenv("YL_STORE_VECTOR_BYTES");
     return (e != nullptr && std::strcmp(e, "32") == 0) ? 32 : 16;
@@ -220,30 +109,12 @@ static int fast_vector_bytes() {
 }
 
 static bool pick_fast(int64_t row_bytes, int w, bool slot64, StoreVariant &out) {
-  if (w == 16) {
-    switch (row_bytes) {
-      case 16: out = make_variant<16, 1, 1, 8>(slot64); return true;
-      case 32: out = make_variant<16, 2, 1, 8>(slot64); return true;
-      case 64: out = make_variant<16, 4, 1, 8>(slot64); return true;
-      case 128: out = make_variant<16, 8, 1, 8>(slot64); return true;
-      case 256: out = make_variant<16, 16, 1, 8>(slot64); return true;
-      case 512: out = make_variant<16, 32, 1, 8>(slot64); return true;
-      case 1024: out = make_variant<16, 32, 2, 4>(slot64); return true;
-      case 2048: out = make_variant<16, 32, 4, 2>(slot64); return true;
-      case 4096: out = make_variant<16, 32, 8, 1>(slot64); return true;
-      case 8192: out = make_variant<16, 32, 16, 1>(slot64); return true;
-      default: return false;
-    }
-  }
-  switch (row_bytes) {
-    case 256: out = make_variant<32, 8, 1, 8>(slot64); return true;
-    case 512: out = make_variant<32, 16, 1, 8>(slot64); return true;
-    case 1024: out = make_variant<32, 32, 1, 4>(slot64); return true;
-    case 2048: out = make_variant<32, 32, 2, 2>(slot64); return true;
-    case 4096: out = make_variant<32, 32, 4, 1>(slot64); return true;
-    case 8192: out = make_variant<32, 32, 8, 1>(slot64); return true;
-    default: return false;
-  }
+  return dispatch_row_shape(row_bytes, w, [&](auto shape) {
+    using S = decltype(shape);
+    out = StoreVariant{slot64 ? store_rows_kernel<S::W, S::G, S::VPL, S::R, int64_t>
+                              : store_rows_kernel<S::W, S::G, S::VPL, S::R, int32_t>,
+                       S::G, S::R};
+  });
 }
 
 static StoreVariant pick_generic(int unit, bool slot64) {
@@ -266,16 +137,16 @@ static int widest_unit(uintptr_t bits) {
 
 constexpr int kStoreThreads = 256;
 
-// Resident blocks per SM of a store kernel on the current device (cached).
-static int blocks_per_sm(StoreKernel fn) {
+// Resident blocks per SM of a kernel at kStoreThreads threads (cached per device).
+int blocks_per_sm(const void *fn, size_t smem) {
   static std::mutex mu;
-  static std::map<std::pair<int, const void *>, int> cache;
-  const std::pair<int, const void *> key{current_device(), reinterpret_cast<const void *>(fn)};
+  static std::map<std::tuple<int, const void *, size_t>, int> cache;
+  const auto key = std::make_tuple(current_device(), fn, smem);
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kStoreThreads, 0) != cudaSuccess || n <= 0) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kStoreThreads, smem) != cudaSuccess || n <= 0) {
     cudaGetLastError();
     n = 1;
   }
@@ -283,17 +154,13 @@ static int blocks_per_sm(StoreKernel fn) {
   return n;
 }
 
-}  // namespace ylk
-
-extern "C" int yl_kv_store(const yl_store_args *a, cudaStream_t stream) {
-  using namespace ylk;
-  clear_last_error();
+int prepare_store(const yl_store_args *a, bool need_slots, StorePlan &plan) {
   if (a == nullptr) return fail(YL_ERR_NULL_ARG, "yl_kv_store: args is NULL");
   if (a->num_tokens < 0) return fail(YL_ERR_BAD_SIZE, "yl_kv_store: num_tokens=%lld < 0", a->num_tokens);
   if (a->num_layers < 1) return fail(YL_ERR_BAD_SIZE, "yl_kv_store: num_layers=%lld < 1", a->num_layers);
   if (a->row_bytes <= 0) return fail(YL_ERR_BAD_SIZE, "yl_kv_store: row_bytes=%lld <= 0", a->row_bytes);
   if (a->num_tokens == 0) return YL_OK;  // MHAKVCache::StoreKV returns early on N == 0
-  if (!a->k || !a->v || !a->k_cache || !a->v_cache || !a->slots)
+  if (!a->k || !a->v || !a->k_cache || !a->v_cache || (need_slots && !a->slots))
     return fail(YL_ERR_NULL_ARG, "yl_kv_store: k, v, k_cache, v_cache and slots must be non-NULL");
   if (a->slot_is_int64 != 0 && a->slot_is_int64 != 1)
     return fail(YL_ERR_BAD_SIZE, "yl_kv_store: slot_is_int64=%lld must be 0 or 1", a->slot_is_int64);
@@ -302,6 +169,9 @@ extern "C" int yl_kv_store(const yl_store_args *a, cudaStream_t stream) {
   const uint64_t total_rows = 2ull * static_cast<uint64_t>(a->num_layers) * static_cast<uint64_t>(a->num_tokens);
   if (total_rows >= (1ull << 31))
     return fail(YL_ERR_UNSUPPORTED, "yl_kv_store: 2*L*N=%lld rows exceeds 2^31-1 per call", (long long)total_rows);
+  const size_t slot_bytes = a->slot_is_int64 ? 8 : 4;
+  if (need_slots && (reinterpret_cast<uintptr_t>(a->slots) & (slot_bytes - 1)) != 0)
+    return fail(YL_ERR_ALIGNMENT, "yl_kv_store: slots pointer is not %lld-byte aligned", (long long)slot_bytes);
 
   const bool multi = a->num_layers > 1;
   uintptr_t bits = reinterpret_cast<uintptr_t>(a->k) | reinterpret_cast<uintptr_t>(a->v) |
@@ -311,12 +181,12 @@ extern "C" int yl_kv_store(const yl_store_args *a, cudaStream_t stream) {
   if (multi)
     bits |= static_cast<uintptr_t>(a->k_layer_stride) | static_cast<uintptr_t>(a->v_layer_stride) |
             static_cast<uintptr_t>(a->cache_layer_stride);
-  const int unit = widest_unit(bits);
-  const size_t slot_bytes = a->slot_is_int64 ? 8 : 4;
-  if ((reinterpret_cast<uintptr_t>(a->slots) & (slot_bytes - 1)) != 0)
-    return fail(YL_ERR_ALIGNMENT, "yl_kv_store: slots pointer is not %lld-byte aligned", (long long)slot_bytes);
+  plan.bits = bits;
+  plan.unit = widest_unit(bits);
+  if (a->row_bytes / plan.unit >= (1ll << 31))
+    return fail(YL_ERR_UNSUPPORTED, "yl_kv_store: row_bytes=%lld too large", a->row_bytes);
 
-  StoreParams p;
+  StoreParams &p = plan.p;
   p.k = static_cast<const char *>(a->k);
   p.v = static_cast<const char *>(a->v);
   p.k_cache = static_cast<char *>(a->k_cache);
@@ -331,25 +201,49 @@ extern "C" int yl_kv_store(const yl_store_args *a, cudaStream_t stream) {
   p.num_slots = a->num_slots;
   p.error_word = a->error_word;
   p.total_rows = static_cast<uint32_t>(total_rows);
-  p.row_units = static_cast<uint32_t>(a->row_bytes / unit);
+  p.row_units = static_cast<uint32_t>(a->row_bytes / plan.unit);
   p.by_tokens = FastDiv(static_cast<uint32_t>(a->num_tokens));
+  return YL_OK;
+}
 
-  const bool slot64 = a->slot_is_int64 != 0;
+int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStream_t stream, bool pdl) {
   StoreVariant var{};
   bool fast = false;
   const int w = fast_vector_bytes();
-  if (unit == 16 && w == 32 && ((bits & 31u) == 0)) fast = pick_fast(a->row_bytes, 32, slot64, var);
-  if (!fast && unit == 16) fast = pick_fast(a->row_bytes, 16, slot64, var);
-  if (!fast) {
-    if (a->row_bytes / unit >= (1ll << 31))
-      return fail(YL_ERR_UNSUPPORTED, "yl_kv_store: row_bytes=%lld too large", a->row_bytes);
-    var = pick_generic(unit, slot64);
-  }
-
+  if (plan.unit == 16 && w == 32 && (plan.bits & 31u) == 0) fast = pick_fast(row_bytes, 32, slot64, var);
+  if (!fast && plan.unit == 16) fast = pick_fast(row_bytes, 16, slot64, var);
+  if (!fast) var = pick_generic(plan.unit, slot64);
   const uint64_t rows_per_block = static_cast<uint64_t>(kStoreThreads / var.group) * var.rows;
-  const uint64_t want = (total_rows + rows_per_block - 1) / rows_per_block;
-  const uint64_t cap = static_cast<uint64_t>(sm_count()) * blocks_per_sm(var.fn);
+  const uint64_t want = (plan.p.total_rows + rows_per_block - 1) / rows_per_block;
+  const uint64_t cap =
+      static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.fn), 0);
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
-  var.fn<<<grid, kStoreThreads, 0, stream>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kStoreThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, var.fn, plan.p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error(std::string("yl_kv_store launch: ") + cudaGetErrorString(e));
+    return YL_ERR_CUDA;
+  }
   return check_launch("yl_kv_store launch");
+}
+
+}  // namespace ylk
+
+extern "C" int yl_kv_store(const yl_store_args *a, cudaStream_t stream) {
+  using namespace ylk;
+  clear_last_error();
+  StorePlan plan;
+  const int rc = prepare_store(a, true, plan);
+  if (rc != YL_OK || a->num_tokens == 0) return rc;
+  return launch_store(plan, a->row_bytes, a->slot_is_int64 != 0, stream, false);
 }

@@ -1,0 +1,124 @@
+// Python bindings of the C++ front end (module yllang_b200._C).
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include "yllang_kvpath.h"
+
+namespace py = pybind11;
+using namespace yllang;
+
+PYBIND11_MODULE(_C, m) {
+  m.doc() = "C++17 libtorch front end of the B200 paged KV store and batch index build";
+  py::register_exception<PanicError>(m, "PanicError", PyExc_RuntimeError);
+
+  m.def(
+      "StoreKVCache",
+      [](const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &kc, const torch::Tensor &vc,
+         const torch::Tensor &idx) { StoreKVCache(k, v, kc, vc, idx); },
+        py::arg("k"), py::arg("v"), py::arg("k_cache"), py::arg("v_cache"), py::arg("indices"),
+        "k_cache[indices[i]] = k[i], v_cache[indices[i]] = v[i] (row size taken at run time)");
+  m.def(
+      "StoreKVCache2048",
+      [](const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &kc, const torch::Tensor &vc,
+         const torch::Tensor &idx) { StoreKVCache<2048>(k, v, kc, vc, idx); },
+      py::arg("k"), py::arg("v"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("indices"),
+        "the reference's StoreKVCache<kElementSize = 2048> signature (row size checked)");
+  m.def("StoreKVCacheLayers", &StoreKVCacheLayers, py::arg("k"), py::arg("v"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("indices"), "every layer of a step in one launch: k, v [L, N, E]");
+
+  m.def("SetDistributedInfo", &SetDistributedInfo, py::arg("rank"), py::arg("size"));
+  m.def("GetDistributedInfo", []() {
+    const auto &d = GetDistributedInfo();
+    return py::make_tuple(d.GetRank(), d.GetSize());
+  });
+
+  py::enum_<KVCacheLayout>(m, "KVCacheLayout")
+      .value("kPageFirst", kPageFirst)
+      .value("kLayerFirst", kLayerFirst)
+      .export_values();
+
+  py::class_<MHAKVCache>(m, "MHAKVCache")
+      .def(py::init([](int num_layers, int num_pages, int num_kv_heads, int head_dim, KVCacheLayout layout,
+                       const std::string &device, py::object dtype, int page_size, bool zero_fill) {
+             const auto st = torch::python::detail::py_object_to_dtype(dtype);
+             return std::make_unique<MHAKVCache>(num_layers, num_pages, num_kv_heads, head_dim, layout,
+                                                 torch::Device(device), st, page_size, zero_fill);
+           }),
+           py::arg("num_layers"), py::arg("num_pages"), py::arg("num_kv_heads"), py::arg("head_dim"),
+           py::arg("kv_layout"), py::arg("device"), py::arg("dtype"), py::arg("page_size") = 1,
+           py::arg("zero_fill") = true)
+      .def("StoreKV", &MHAKVCache::StoreKV, py::arg("k"), py::arg("v"), py::arg("loc"), py::arg("layer_id"))
+      .def("StoreKVAllLayers", &MHAKVCache::StoreKVAllLayers, py::arg("k"), py::arg("v"), py::arg("loc"))
+      .def("KCache", &MHAKVCache::KCache)
+      .def("VCache", &MHAKVCache::VCache)
+      .def("NumLayers", &MHAKVCache::NumLayers)
+      .def("Device", [](MHAKVCache &c) { return c.Device().str(); })
+      .def("PageSize", &MHAKVCache::PageSize)
+      .def("NumPages", &MHAKVCache::NumPages)
+      .def("NumLocalKVHeads", &MHAKVCache::NumLocalKVHeads)
+      .def("HeadDim", &MHAKVCache::HeadDim)
+      .def("NumSlots", &MHAKVCache::NumSlots)
+      .def("Buffer", &MHAKVCache::Buffer);
+
+  py::class_<BatchIndex>(m, "BatchIndex")
+      .def_readonly("kv_indptr", &BatchIndex::kv_indptr)
+      .def_readonly("kv_indices", &BatchIndex::kv_indices)
+      .def_readonly("kv_last_page_len", &BatchIndex::kv_last_page_len)
+      .def_readonly("qo_indptr", &BatchIndex::qo_indptr)
+      .def_readonly("slot_mapping", &BatchIndex::slot_mapping);
+
+  m.def(
+      "BuildBatchIndex",
+      [](const torch::Tensor &prior_len, const torch::Tensor &new_len, const torch::Tensor &page_table, int page_size,
+         std::optional<torch::Tensor> table_index, int64_t num_pages, int64_t kv_indices_capacity,
+         int64_t slot_capacity, bool slot_int64, std::optional<torch::Tensor> error_word) {
+        return BuildBatchIndex(prior_len, new_len, page_table, page_size, table_index, num_pages,
+                               kv_indices_capacity, slot_capacity, slot_int64 ? torch::kInt64 : torch::kInt32,
+                               error_word);
+      },
+      py::arg("prior_len"), py::arg("new_len"), py::arg("page_table"), py::arg("page_size"),
+      py::arg("table_index") = py::none(), py::arg("num_pages") = 0, py::arg("kv_indices_capacity") = -1,
+      py::arg("slot_capacity") = -1, py::arg("slot_int64") = true, py::arg("error_word") = py::none());
+
+  py::class_<KVCacheManager, std::shared_ptr<KVCacheManager>>(m, "KVCacheManager")
+      .def(py::init([](int64_t num_pages, int64_t max_requests, int64_t max_pages_per_request, int page_size,
+                       const std::string &device) {
+             return std::make_shared<KVCacheManager>(num_pages, max_requests, max_pages_per_request, page_size,
+                                                     torch::Device(device));
+           }),
+           py::arg("num_pages"), py::arg("max_requests"), py::arg("max_pages_per_request"), py::arg("page_size"),
+           py::arg("device"))
+      .def("NumPages", &KVCacheManager::NumPages)
+      .def("PageSize", &KVCacheManager::PageSize)
+      .def("RemainingPageCount", &KVCacheManager::RemainingPageCount)
+      .def("RemainingTableSlots", &KVCacheManager::RemainingTableSlots)
+      .def("AllocateTableSlot", &KVCacheManager::AllocateTableSlot)
+      .def("AllocatePages", &KVCacheManager::AllocatePages)
+      .def("FreePages", &KVCacheManager::FreePages)
+      .def("Reserve", &KVCacheManager::Reserve)
+      .def("Release", &KVCacheManager::Release)
+      .def("PagesInRow", &KVCacheManager::PagesInRow)
+      .def("SyncPageTable", &KVCacheManager::SyncPageTable)
+      .def("PageTable", &KVCacheManager::PageTable)
+      .def("HostPageTable", &KVCacheManager::HostPageTable);
+
+  py::class_<RequestSlot>(m, "RequestSlot")
+      .def(py::init<int64_t, int64_t, int64_t>(), py::arg("table_index"), py::arg("cached_len"),
+           py::arg("device_len"))
+      .def_readwrite("table_index", &RequestSlot::table_index)
+      .def_readwrite("cached_len", &RequestSlot::cached_len)
+      .def_readwrite("device_len", &RequestSlot::device_len);
+
+  py::class_<Batch>(m, "Batch")
+      .def_readonly("index", &Batch::index)
+      .def_readonly("table_index", &Batch::table_index)
+      .def_readonly("num_tokens", &Batch::num_tokens)
+      .def_property_readonly("out_loc", [](const Batch &b) { return b.index.slot_mapping; });
+
+  py::class_<BatchManager>(m, "BatchManager")
+      .def(py::init<std::shared_ptr<KVCacheManager>>(), py::arg("cache"))
+      .def("NextBatch", &BatchManager::NextBatch, py::arg("requests"))
+      .def("Cache", &BatchManager::Cache);
+}

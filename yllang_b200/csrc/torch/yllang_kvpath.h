@@ -1,0 +1,238 @@
+// C++17 libtorch front end of the paged KV store and batch index build.
+//
+// Same names, argument meanings and error behaviour as the reference's
+// interfaces on this path, so YLLang-style callers drop in:
+//   StoreKVCache<kElementSize>   src/include/kvcache/store_kv_cache.h:29-31
+//   BaseKVCache / MHAKVCache     src/include/kvcache/base_kvcache.h:26-70,
+//                                src/include/kvcache/mha_kvcache.h:25-148
+//   DistributedInfo              src/include/distributed/info.h:18-66
+//   KVCacheManager (pages)       src/include/kvcache/cache_manager.h:21-185
+//   BatchManager::NextBatch      src/include/batch/batch_manager.h:83-115
+// Every device operation goes through the C ABI of libyl_kvpath.so
+// (include/yl_kvpath.h) on the current c10 CUDA stream; contract violations
+// throw PanicError before any launch, as RuntimeCheck does in the reference.
+#pragma once
+
+#include <torch/torch.h>
+
+#include <cstdint>
+#include <memory>
+#include <optional>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace yllang {
+
+class PanicError final : public std::runtime_error {
+ public:
+  explicit PanicError(const std::string &msg) : std::runtime_error(msg) {}
+};
+
+// Throws PanicError(msg) when cond is false.
+void RuntimeCheck(bool cond, const std::string &msg);
+
+// ----------------------------------------------------------------------------
+// Store
+// ----------------------------------------------------------------------------
+
+// k_cache[indices[i]] <- k[i], v_cache[indices[i]] <- v[i] for i < N, with the
+// row size taken at run time.  Shapes as the reference's TensorMatcher
+// enforces (store_kv_cache.cu:108-124): caches [S, E] with stride [cs, 1],
+// k/v [N, E] with stride [ks, 1], indices [N] int32 or int64 with stride 1,
+// one device, one dtype.  An empty batch is a no-op.
+void StoreKVCache(const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &k_cache,
+                  const torch::Tensor &v_cache, const torch::Tensor &indices);
+
+// The reference's compile-time-row-size signature; checks
+// kElementSize == E * itemsize (store_kv_cache.cu:136) and forwards.
+template <size_t kElementSize, size_t kThreadsPreBlock = 128, bool kUsePDL = false>
+void StoreKVCache(const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &k_cache,
+                  const torch::Tensor &v_cache, const torch::Tensor &indices) {
+  RuntimeCheck(k.dim() == 2 && static_cast<size_t>(k.size(1) * k.element_size()) == kElementSize,
+               "StoreKVCache: kElementSize != row elements * dtype size");
+  StoreKVCache(k, v, k_cache, v_cache, indices);
+}
+
+// Every layer of one step in one launch: k/v [L, N, E], caches [L, S, E].
+void StoreKVCacheLayers(const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &k_cache,
+                        const torch::Tensor &v_cache, const torch::Tensor &indices);
+
+// ----------------------------------------------------------------------------
+// Tensor-parallel rank info (only the head split uses it)
+// ----------------------------------------------------------------------------
+class DistributedInfo {
+ public:
+  DistributedInfo(int rank, int size) noexcept : m_rank_(rank), m_size_(size) {}
+  int GetRank() const { return m_rank_; }
+  int GetSize() const { return m_size_; }
+  void SetRank(int rank) { m_rank_ = rank; }
+  void SetSize(int size) { m_size_ = size; }
+
+ private:
+  int m_rank_;
+  int m_size_;
+};
+DistributedInfo &GetDistributedInfo();
+void SetDistributedInfo(int rank, int size);
+
+// ----------------------------------------------------------------------------
+// KV cache
+// ----------------------------------------------------------------------------
+enum KVCacheLayout : std::uint8_t { kPageFirst = 0, kLayerFirst };
+
+class BaseKVCache {
+ public:
+  BaseKVCache() = default;
+  virtual ~BaseKVCache() = default;
+  virtual void StoreKV(torch::Tensor k, torch::Tensor v, torch::Tensor loc, int layer_id) = 0;
+  virtual torch::Tensor KCache(int layer_id) = 0;
+  virtual torch::Tensor VCache(int layer_id) = 0;
+  virtual int NumLayers() = 0;
+  virtual torch::Device Device() = 0;
+};
+
+// Paged pool [2, L, P, page_size, H_local, D] (layer-major NHD, the layout
+// both of the reference's KVCacheLayout values end up with, mha_kvcache.h:53-58),
+// H_local = num_kv_heads / tp size.  A slot is page * page_size + offset; the
+// per-layer views are [P, page_size, H_local, D] (what a flashinfer NHD paged
+// call takes).  page_size defaults to 1 as in the reference
+// (mha_kvcache.h:144).
+class MHAKVCache : public BaseKVCache {
+ public:
+  MHAKVCache(int num_layers, int num_pages, int num_kv_heads, int head_dim, KVCacheLayout kv_layout,
+             torch::Device device, torch::Dtype dtype, int page_size = 1, bool zero_fill = true);
+
+  // Per-layer store (the reference's call): k, v [..., H_local, D] with N rows.
+  void StoreKV(torch::Tensor k, torch::Tensor v, torch::Tensor loc, int layer_id) override;
+  // All layers at once: k, v [L, N, H_local * D] (or [L, N, H_local, D]).
+  void StoreKVAllLayers(torch::Tensor k, torch::Tensor v, torch::Tensor loc);
+
+  torch::Tensor KCache(int layer_id) override;
+  torch::Tensor VCache(int layer_id) override;
+  int NumLayers() override { return m_num_layers_; }
+  torch::Device Device() override { return m_device_; }
+
+  int PageSize() const { return m_page_size_; }
+  int NumPages() const { return m_num_pages_; }
+  int NumLocalKVHeads() const { return m_num_local_kv_heads_; }
+  int HeadDim() const { return m_head_dim_; }
+  int64_t NumSlots() const { return static_cast<int64_t>(m_num_pages_) * m_page_size_; }
+  torch::Tensor Buffer() const { return m_buffer_; }
+
+ private:
+  torch::Tensor m_buffer_;    // [2, L, P, ps, H_local, D]
+  torch::Tensor m_k_rows_;    // [L, P*ps, H_local*D] view of K
+  torch::Tensor m_v_rows_;    // [L, P*ps, H_local*D] view of V
+  int m_num_layers_;
+  int m_num_pages_;
+  int m_num_local_kv_heads_{0};
+  int m_head_dim_;
+  int m_page_size_;
+  torch::Device m_device_;
+};
+
+// ----------------------------------------------------------------------------
+// Index build
+// ----------------------------------------------------------------------------
+struct BatchIndex {
+  torch::Tensor kv_indptr;         // int32 [B+1]
+  torch::Tensor kv_indices;        // int32 [sum of pages]
+  torch::Tensor kv_last_page_len;  // int32 [B]
+  torch::Tensor qo_indptr;         // int32 [B+1]
+  torch::Tensor slot_mapping;      // int64 (or int32) [sum of new tokens]
+};
+
+// Device tensors in, device tensors out (see yl_build_index).  When the
+// capacities are negative they are computed from the lengths, which reads
+// the lengths back to the host.
+BatchIndex BuildBatchIndex(const torch::Tensor &prior_len, const torch::Tensor &new_len,
+                           const torch::Tensor &page_table, int page_size,
+                           const std::optional<torch::Tensor> &table_index, int64_t num_pages,
+                           int64_t kv_indices_capacity = -1, int64_t slot_capacity = -1,
+                           torch::Dtype slot_dtype = torch::kInt64,
+                           const std::optional<torch::Tensor> &error_word = std::nullopt);
+
+// ----------------------------------------------------------------------------
+// Page allocator + page table (host free lists, device page table)
+// ----------------------------------------------------------------------------
+// Plays the role of the reference's KVCacheManager (cache_manager.h:21-185)
+// for pages of page_size tokens: free page ids and free table rows are host
+// stacks; the page table [max_requests, max_pages_per_request] int32 lives on
+// the device, with a host mirror whose changed entries are pushed to the
+// device once per batch.  Differences from the reference, which are fixes of
+// its defects: page ids 0..num_pages-1 (torch::range is end-inclusive,
+// cache_manager.h:33-34), allocated pages leave the free list
+// (cache_manager.h:123-124), page ids go into the page table
+// (cache_manager.h:153 writes the token pool).
+class KVCacheManager {
+ public:
+  KVCacheManager(int64_t num_pages, int64_t max_requests, int64_t max_pages_per_request, int page_size,
+                 torch::Device device);
+
+  int64_t NumPages() const { return m_num_pages_; }
+  int PageSize() const { return m_page_size_; }
+  int64_t RemainingPageCount() const { return static_cast<int64_t>(m_free_pages_.size()); }
+  int64_t RemainingTableSlots() const { return static_cast<int64_t>(m_free_rows_.size()); }
+
+  int64_t AllocateTableSlot();             // throws c10::Error when none is left
+  torch::Tensor AllocatePages(int64_t n);  // int32 CPU tensor of n page ids
+  void FreePages(const torch::Tensor &pages);
+
+  // Make row `table_index` hold ceil(tokens / page_size) pages, allocating the
+  // missing ones; returns the pages newly added.
+  torch::Tensor Reserve(int64_t table_index, int64_t tokens);
+  // Free every page of the row and the row itself.
+  void Release(int64_t table_index);
+  int64_t PagesInRow(int64_t table_index) const;
+
+  // Push host-side page-table changes to the device (asynchronous, current stream).
+  void SyncPageTable();
+  torch::Tensor PageTable() const { return m_page_table_; }  // device [R, W] int32
+  torch::Tensor HostPageTable() const { return m_host_table_; }
+
+ private:
+  int64_t m_num_pages_;
+  int64_t m_max_requests_;
+  int64_t m_max_pages_;
+  int m_page_size_;
+  torch::Device m_device_;
+  std::vector<int32_t> m_free_pages_;
+  std::vector<int64_t> m_free_rows_;
+  std::vector<int64_t> m_row_pages_;      // pages held by each row
+  std::vector<int64_t> m_dirty_;          // flat entries of the host table changed since the last sync
+  torch::Tensor m_host_table_;            // CPU int32 [R, W]
+  torch::Tensor m_page_table_;            // device int32 [R, W]
+};
+
+// One request in a batch: the reference Request's table_index, cached_len
+// and device_len (src/include/request/request.h:81-92).
+struct RequestSlot {
+  int64_t table_index;
+  int64_t cached_len;
+  int64_t device_len;
+};
+
+struct Batch {
+  BatchIndex index;            // page arrays for attention + slot mapping (out_loc)
+  torch::Tensor table_index;   // int32 [B] on the device
+  int64_t num_tokens{0};       // sum of device_len - cached_len
+};
+
+// Per-step index driver: reserves pages for every request's new tokens,
+// pushes the page-table changes, stages the lengths in one host-to-device
+// copy and launches the index build.  All device work is asynchronous on the
+// current stream.
+class BatchManager {
+ public:
+  explicit BatchManager(std::shared_ptr<KVCacheManager> cache) : m_cache_(std::move(cache)) {}
+  Batch NextBatch(const std::vector<RequestSlot> &requests);
+  std::shared_ptr<KVCacheManager> Cache() const { return m_cache_; }
+
+ private:
+  std::shared_ptr<KVCacheManager> m_cache_;
+  torch::Tensor m_host_stage_;    // pinned int32 [3, capacity]
+  torch::Tensor m_device_stage_;  // device int32 [3, capacity]
+};
+
+}  // namespace yllang

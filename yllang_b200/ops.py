@@ -106,6 +106,33 @@ class BatchIndex(NamedTuple):
     slot_mapping: torch.Tensor
 
 
+def _check_index_inputs(prior_len, new_len, page_table, table_index) -> None:
+    dev = prior_len.device
+    _check(prior_len.is_cuda, "prior_len must be a CUDA tensor")
+    for name, t in (("prior_len", prior_len), ("new_len", new_len), ("page_table", page_table)):
+        _check(t.dtype == torch.int32, f"{name} must be int32, got {t.dtype}")
+        _check(t.device == dev, f"{name} on {t.device}, expected {dev}")
+    B = prior_len.shape[0]
+    _check(prior_len.dim() == 1 and new_len.shape == (B,), "prior_len and new_len must both be [B]")
+    _check(prior_len.is_contiguous() and new_len.is_contiguous(), "lengths must be contiguous")
+    _check(page_table.dim() == 2 and page_table.stride(1) == 1, "page_table must be [R, W] with unit column stride")
+    if table_index is not None:
+        _check(table_index.dtype == torch.int32 and table_index.shape == (B,) and table_index.is_contiguous()
+               and table_index.device == dev, "table_index must be contiguous int32 [B] on the same device")
+    else:
+        _check(page_table.shape[0] >= B, f"page_table has {page_table.shape[0]} rows for a batch of {B}")
+
+
+def _check_out(out: "BatchIndex", B: int, dev) -> None:
+    for name in ("kv_indptr", "kv_indices", "kv_last_page_len", "qo_indptr"):
+        t = getattr(out, name)
+        _check(t.dtype == torch.int32 and t.device == dev and t.is_contiguous(), f"out.{name}: contiguous int32")
+    _check(out.kv_indptr.numel() >= B + 1 and out.qo_indptr.numel() >= B + 1, "out indptrs need B + 1 entries")
+    _check(out.kv_last_page_len.numel() >= B, "out.kv_last_page_len needs B entries")
+    _check(out.slot_mapping.dtype in (torch.int32, torch.int64) and out.slot_mapping.is_contiguous()
+           and out.slot_mapping.device == dev, "out.slot_mapping: contiguous int32 or int64")
+
+
 def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torch.Tensor, page_size: int,
                 table_index: torch.Tensor | None = None, num_pages: int = 0, kv_indices_capacity: int | None = None,
                 slot_capacity: int | None = None, slot_dtype: torch.dtype = torch.int64,
@@ -118,23 +145,12 @@ def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torc
     when omitted they are computed from the lengths, which costs a device to
     host read (pass them, or `out`, on a hot path).
     """
+    _check_index_inputs(prior_len, new_len, page_table, table_index)
     dev = prior_len.device
-    _check(prior_len.is_cuda, "prior_len must be a CUDA tensor")
-    for name, t in (("prior_len", prior_len), ("new_len", new_len), ("page_table", page_table)):
-        _check(t.dtype == torch.int32, f"{name} must be int32, got {t.dtype}")
-        _check(t.device == dev, f"{name} on {t.device}, expected {dev}")
     B = prior_len.shape[0]
-    _check(prior_len.dim() == 1 and new_len.shape == (B,), "prior_len and new_len must both be [B]")
-    _check(prior_len.is_contiguous() and new_len.is_contiguous(), "lengths must be contiguous")
-    _check(page_table.dim() == 2 and page_table.stride(1) == 1, "page_table must be [R, W] with unit column stride")
-    if table_index is not None:
-        _check(table_index.dtype == torch.int32 and table_index.shape == (B,) and table_index.is_contiguous(),
-               "table_index must be contiguous int32 [B]")
-    else:
-        _check(page_table.shape[0] >= B, f"page_table has {page_table.shape[0]} rows for a batch of {B}")
-    _check(slot_dtype in (torch.int32, torch.int64), "slot_dtype must be int32 or int64")
     W = page_table.shape[1]
     if out is None:
+        _check(slot_dtype in (torch.int32, torch.int64), "slot_dtype must be int32 or int64")
         if kv_indices_capacity is None or slot_capacity is None:
             tot = prior_len.clamp(min=0).to(torch.int64) + new_len.clamp(min=0).to(torch.int64)
             if kv_indices_capacity is None:
@@ -145,15 +161,24 @@ def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torc
         out = BatchIndex(torch.empty(B + 1, **i32), torch.empty(kv_indices_capacity, **i32),
                          torch.empty(B, **i32), torch.empty(B + 1, **i32),
                          torch.empty(slot_capacity, dtype=slot_dtype, device=dev))
+    _check_out(out, B, dev)
+    a = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, error_word)
+    _abi.check(_abi.build_index_raw(a, _stream(stream, dev)))
+    return out
+
+
+def index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out: BatchIndex,
+               error_word) -> _abi.IndexArgs:
+    """Pack validated index tensors into yl_index_args."""
     a = _abi.IndexArgs()
     a.prior_len, a.new_len = prior_len.data_ptr(), new_len.data_ptr()
     a.page_table = page_table.data_ptr()
     a.table_index = table_index.data_ptr() if table_index is not None else None
     a.page_table_stride = page_table.stride(0)
     a.num_table_rows = page_table.shape[0]
-    a.max_pages_per_row = W
+    a.max_pages_per_row = page_table.shape[1]
     a.page_size = page_size
-    a.batch_size = B
+    a.batch_size = prior_len.shape[0]
     a.slot_is_int64 = int(out.slot_mapping.dtype == torch.int64)
     a.num_pages = num_pages
     a.kv_indptr, a.kv_indices = out.kv_indptr.data_ptr(), out.kv_indices.data_ptr()
@@ -162,5 +187,28 @@ def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torc
     a.kv_indices_capacity = out.kv_indices.numel()
     a.slot_capacity = out.slot_mapping.numel()
     a.error_word = error_word.data_ptr() if error_word is not None else None
-    _abi.check(_abi.build_index_raw(a, _stream(stream, dev)))
+    return a
+
+
+def kv_step(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torch.Tensor, page_size: int,
+            k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, out: BatchIndex,
+            table_index: torch.Tensor | None = None, num_pages: int = 0, error_word: torch.Tensor | None = None,
+            stream: torch.cuda.Stream | None = None) -> BatchIndex:
+    """One step: build_index(...) into `out`, then store_kv_cache(k, v,
+    k_cache, v_cache, out.slot_mapping), fused into one launch (yl_kv_step).
+
+    k, v are [N, E] (one layer) or [L, N, E] (every layer); k_cache, v_cache
+    the matching per-layer [S, E] or all-layer [L, S, E] pool views; N must
+    equal the sum of new_len.  `out` must have room for the batch's pages and
+    at least N slots (its slot dtype decides the slot type).
+    """
+    _check(out is not None, "kv_step needs preallocated outputs (out=)")
+    _check_index_inputs(prior_len, new_len, page_table, table_index)
+    _check_out(out, prior_len.shape[0], prior_len.device)
+    N = k.shape[-2]
+    _check(out.slot_mapping.numel() >= N, f"out.slot_mapping holds {out.slot_mapping.numel()} < N={N} slots")
+    a = _abi.StepArgs()
+    a.store = store_args(k, v, k_cache, v_cache, out.slot_mapping[:N], None)
+    a.index = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, error_word)
+    _abi.check(_abi.kv_step_raw(a, _stream(stream, k.device)))
     return out

@@ -1,11 +1,11 @@
 """Seeded synthetic batches for the store + index path.
 
 Each generator returns a `Batch` of per-sequence lengths and page-table rows
-with the shapes of one serving workload; K/V rows are drawn separately
-(`make_kv`).  Seeds: lengths from numpy default_rng(seed_len=1), page ids
-from default_rng(seed_pages=2), K/V from torch seed 0, values N(0, 1) cast to
-the K/V dtype.  Page tables are randomly fragmented: consecutive pages of a
-sequence are unrelated pool pages.
+with the shapes of one serving workload; callers draw the K/V rows (N(0, 1)
+cast to the K/V dtype, from a seeded torch generator).  Seeds: lengths from
+numpy default_rng(seed_len=1), page ids from default_rng(seed_pages=2).  Page
+tables are randomly fragmented: consecutive pages of a sequence are
+unrelated pool pages.
 
 Workloads (num_pages is chosen by the caller to fit its memory):
   cpu_ref         1 layer, 8 KV heads x 128, page 16; priors 17/33/64/100 + 1
@@ -68,6 +68,12 @@ class Batch:
     def store_bytes(self) -> int:
         """Algorithmic bytes of one step's store: read + write of every K and V row, plus the slots."""
         return self.tokens * self.layers * 2 * 2 * self.row_bytes + self.tokens * 8
+
+    def step_bytes(self, slot_bytes: int = 8) -> int:
+        """Algorithmic bytes of one fused step: every K/V row read and written
+        once, plus the index build's inputs and outputs (the slots are
+        computed, not read back)."""
+        return self.tokens * self.layers * 2 * 2 * self.row_bytes + self.index_bytes(slot_bytes)
 
     def index_bytes(self, slot_bytes: int = 8) -> int:
         """Algorithmic bytes of one index build (lengths, page-table reads, all five outputs)."""
