@@ -285,25 +285,30 @@ def load_peaks():
 # ---------------------------------------------------------------------------
 def cpu_store_step_sample(b: workloads.Batch, seconds: float, threads: int | None = None):
     """Time the oracle's index build + store of this batch on the host cores
-    for about `seconds`, with the pool scaled down to 4 GB of host memory."""
+    for about `seconds`, the pool scaled to 4 GB of host memory and the inputs
+    rotating over sets larger than the last-level cache."""
     from oracle import kvpath as orc
 
     threads = threads or orc.max_threads()
-    hb, pool, k, v = host_step_setup(b)
-    host_step(hb, pool, k, v, threads)  # first touch of the pool pages
+    sets, pool = host_step_setup(b)
+    for hb, k, v in sets:  # first touch of the pool pages and of every input set
+        host_step(hb, pool, k, v, threads)
     reps, t0 = 0, time.perf_counter()
     while True:
+        hb, k, v = sets[reps % len(sets)]
         host_step(hb, pool, k, v, threads)
         reps += 1
         el = time.perf_counter() - t0
         if el >= seconds and reps >= 3:
             break
     per_step = el / reps
+    hb = sets[0][0]
     gbs = hb.store_bytes() / per_step / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{reps} full steps of {hb.name} (B={hb.batch}, N={hb.tokens}, L={hb.layers}, "
                       f"row {hb.row_bytes} B) into a {pool.nbytes / 1e9:.1f} GB host pool, index build + store, "
-                      f"C oracle on {threads} threads",
+                      f"C oracle on {threads} threads, inputs rotating over {len(sets)} sets "
+                      f"({len(sets) * 2 * hb.layers * hb.tokens * hb.row_bytes / 1e6:.0f} MB)",
             "ms_per_step": round(per_step * 1e3, 3)}
 
 
@@ -338,23 +343,36 @@ def ref_make2d_us(b: workloads.Batch, max_seconds: float = 5.0):
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
+HOST_ROTATE_BYTES = 600e6  # host input sets cycled through: more than a server's last-level cache
+
+
 def host_step_setup(b: workloads.Batch, pool_gb: float = 4.0):
-    """The batch re-drawn for a host pool of pool_gb (same shapes; read-only
-    pages alias, written pages unique) plus its K/V rows as raw bf16 bits."""
+    """Host copies of the batch for the CPU arm: the pool scaled down to
+    pool_gb (same row and page size; read-only pages alias, written pages
+    stay unique) and enough input sets -- K/V rows as raw bf16 bits, page
+    tables with their own page ids -- that one pass over them (> 600 MB) does
+    not fit a CPU's last-level cache, as the GPU arm rotates past its L2."""
     P = max(workloads.pool_pages_for(pool_gb * 1e9, b.layers, b.row_bytes, b.page_size), b.tokens + 1)
-    if b.name == "llama3_decode":
-        hb = workloads.llama3_decode(P, batch=b.batch, kv_heads=b.kv_heads, layers=b.layers)
-    elif b.name == "ragged_prefill":
-        hb = workloads.ragged_prefill(P, requests=b.batch, kv_heads=b.kv_heads, layers=b.layers)
-    else:
-        hb = b
-    S = hb.num_pages * hb.page_size
-    E = hb.kv_heads * hb.head_dim
-    pool = np.zeros((2, hb.layers, S, E), np.uint16)
-    rng = np.random.default_rng(0)
-    k = rng.integers(0, 1 << 16, (hb.layers, hb.tokens, E), dtype=np.uint16)
-    v = rng.integers(0, 1 << 16, (hb.layers, hb.tokens, E), dtype=np.uint16)
-    return hb, pool, k, v
+    per_set = 2 * b.layers * b.tokens * b.row_bytes
+    R = max(1, min(16, int(math.ceil(HOST_ROTATE_BYTES / per_set))))
+    sets = []
+    for r in range(R):
+        if b.name == "llama3_decode":
+            hb = workloads.llama3_decode(P, batch=b.batch, kv_heads=b.kv_heads, layers=b.layers, seed_pages=2 + r)
+        elif b.name == "ragged_prefill":
+            hb = workloads.ragged_prefill(P, requests=b.batch, kv_heads=b.kv_heads, layers=b.layers,
+                                          seed_pages=2 + r)
+        else:
+            hb = b
+        E = hb.kv_heads * hb.head_dim
+        rng = np.random.default_rng(r)
+        n = hb.layers * hb.tokens * E
+        k = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
+        v = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
+        sets.append((hb, k, v))
+    hb = sets[0][0]
+    pool = np.zeros((2, hb.layers, hb.num_pages * hb.page_size, hb.kv_heads * hb.head_dim), np.uint16)
+    return sets, pool
 
 
 def host_step(hb, pool, k, v, threads):
@@ -371,11 +389,13 @@ def run_reference(args, world, rank):
     batches, desc = make_batches(args.workload, 1, 150e9, 1)
     b = batches[0]
     threads = orc.max_threads()
-    hb, pool, k, v = host_step_setup(b)
+    sets, pool = host_step_setup(b)
+    hb = sets[0][0]
     times = []
     for it in range(args.warmup + args.steps):
+        s_hb, k, v = sets[it % len(sets)]
         t0 = time.perf_counter()
-        host_step(hb, pool, k, v, threads)
+        host_step(s_hb, pool, k, v, threads)
         if it >= args.warmup:
             times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
@@ -389,8 +409,9 @@ def run_reference(args, world, rank):
         "tokens_per_s": round(hb.tokens / per, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"each step: index build + store of {hb.name} (B={hb.batch}, N={hb.tokens}, "
-                                   f"L={hb.layers}) into a {pool.nbytes / 1e9:.1f} GB host pool by the C oracle; "
-                                   "the reference's store exists only as a CUDA kernel"},
+                                   f"L={hb.layers}) into a {pool.nbytes / 1e9:.1f} GB host pool by the C oracle, "
+                                   f"inputs rotating over {len(sets)} sets; the reference's store exists only as "
+                                   "a CUDA kernel"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     mk = ref_make2d_us(b, max_seconds=5.0)

@@ -68,6 +68,7 @@ typedef enum yl_status {
 #define YL_DEVERR_INDPTR_OVERFLOW 0x40u /* index: a running sum passed INT32_MAX (no fill)  */
 #define YL_DEVERR_TABLE_ROW       0x80u /* index: table_index outside [0, num_table_rows)   */
 #define YL_DEVERR_TOKEN_COUNT     0x100u /* step: sum of new_len differs from num_tokens      */
+#define YL_DEVERR_TIMEOUT         0x200u /* store: a bulk copy did not complete within 2 s    */
 
 /*
  * Store (replaces yllang::StoreKVCache<kElementSize>,

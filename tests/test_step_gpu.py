@@ -148,3 +148,19 @@ def test_step_bad_page_skips_rows(cuda):
     assert int(err.item()) == want["err"] and want["err"] & orc.PAGE_RANGE
     assert np.array_equal(out.slot_mapping.cpu().numpy(), want["slot_mapping"])
     assert int((kc.view(torch.int16) != 0).any(dim=1).sum()) == int((want["slot_mapping"] >= 0).sum())
+
+
+@pytest.mark.parametrize("mode", ["tma", "fused", "serial"])
+def test_step_other_modes(cuda, mode):
+    """The TMA-staged and register-staged fused kernels and the serial
+    two-launch form give the same results as the default PDL-overlapped form
+    (the mode is read once per process, so run in a child)."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, YL_STEP_MODE=mode)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(here, "test_step_gpu.py"), "-k", "not other_modes"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

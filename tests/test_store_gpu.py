@@ -175,8 +175,8 @@ def test_store_workload_slots(cuda, make):
     assert int(kc[:, ~written].view(torch.int16).abs().sum()) == 0
 
 
-def test_store_vector32_variant_matches(cuda):
-    """The 32-byte-vector fast path (YL_STORE_VECTOR_BYTES=32) is bit-exact too."""
+def test_store_vector16_variant_matches(cuda):
+    """The 16-byte-vector fast path (YL_STORE_VECTOR_BYTES=16) is bit-exact too."""
     code = (
         "import sys; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
         "import torch, numpy as np, yllang_b200 as yl\n"
@@ -193,6 +193,19 @@ def test_store_vector32_variant_matches(cuda):
         "    yl.store_kv_cache(k, v, kc, vc, s); torch.cuda.synchronize()\n"
         "    assert np.array_equal(host_bytes(kc), wk) and np.array_equal(host_bytes(vc), wv), (rb, L)\n"
         "print('ok')\n" % (ROOT, os.path.join(ROOT, "tests")))
-    env = dict(os.environ, YL_STORE_VECTOR_BYTES="32")
+    env = dict(os.environ, YL_STORE_VECTOR_BYTES="16")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("env", [{"YL_STORE_ENGINE": "tma"}, {"YL_STORE_ENGINE": "tma", "YL_STEP_MODE": "serial"}])
+def test_store_engines_match(cuda, env):
+    """The TMA-staged store engine passes the store and step suites too (the
+    engine is read once per process, so run them in a child)."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(here, "test_store_gpu.py"), os.path.join(here, "test_step_gpu.py"),
+                        os.path.join(here, "test_ref_kernel_gpu.py"),
+                        "-k", "not engines_match and not other_modes and not vector16"],
+                       env=dict(os.environ, **env), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

@@ -29,6 +29,7 @@ DEVERR_NEGATIVE_LEN = 0x20
 DEVERR_INDPTR_OVERFLOW = 0x40
 DEVERR_TABLE_ROW = 0x80
 DEVERR_TOKEN_COUNT = 0x100
+DEVERR_TIMEOUT = 0x200
 
 ABI_VERSION = 1
 

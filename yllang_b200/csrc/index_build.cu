@@ -78,6 +78,9 @@ static int ensure_smem_attr() {
   std::lock_guard<std::mutex> lock(mu);
   if (static_cast<int>(done.size()) <= dev) done.resize(dev + 1, 0);
   if (!done[dev]) {
+    // No carveout preference: the store kernel that runs as this kernel's PDL
+    // dependent takes the default split too, so both fit on one SM at once (a
+    // differing preference keeps the store's blocks off an SM until it drains).
     const cudaError_t e = cudaFuncSetAttribute(build_index_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(single_launch_smem(kSmemBatchLimit)));
     if (e != cudaSuccess) {
@@ -138,6 +141,7 @@ int prepare_index(const yl_index_args *a, IndexParams &p) {
   p.batch = a->batch_size;
   p.slot64 = a->slot_is_int64;
   p.by_page = FastDiv(static_cast<uint32_t>(a->page_size));
+  p.expected_tokens = -1;
 
   return YL_OK;
 }

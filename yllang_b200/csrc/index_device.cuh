@@ -36,6 +36,7 @@ struct IndexParams {
   int32_t batch;
   int32_t slot64;
   FastDiv by_page;
+  int64_t expected_tokens;  // step only: the store's N, checked against the sum of new_len (-1: no check)
 };
 
 struct SeqFacts {
@@ -185,7 +186,7 @@ __device__ __forceinline__ void write_slot(const IndexParams &p, int64_t t, int6
   else static_cast<int32_t *>(p.slot_mapping)[t] = static_cast<int32_t>(slot);
 }
 
-// kv_indices[e] for one element e < kv_indptr[B].
+// kv_indices[e] for one element e < kv_indptr[B] (the fused step kernels).
 __device__ __forceinline__ void kv_index_elem(const IndexParams &p, const int32_t *kvp, int64_t e) {
   const int i = find_seq(kvp, p.batch, e);
   const int64_t col = e - kvp[i];
@@ -216,16 +217,48 @@ __device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_
 
 // Phase C for the elements [begin, end) of [kv_indices | slot_mapping].  Slot
 // entries past qo_indptr[B] (up to the slot capacity) are written as -1.
+// Each thread gathers kFillUnroll elements per pass with independent chains
+// (search, page-table read), so their global reads are in flight together.
 // Each element belongs to exactly one block, so every block reports its own.
+constexpr int kFillUnroll = 4;
+
 __device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, const int32_t *qop, int64_t n_idx,
-                           int64_t begin, int64_t end) {
+                                  int64_t begin, int64_t end) {
   const int64_t n_tok = qop[p.batch];
-  for (int64_t e = begin + threadIdx.x; e < end; e += blockDim.x) {
-    if (e < n_idx) {
-      kv_index_elem(p, kvp, e);
-    } else {
-      const int64_t t = e - n_idx;
-      write_slot(p, t, t < n_tok ? token_slot(p, kvp, qop, t) : -1);
+  const int64_t step = static_cast<int64_t>(blockDim.x) * kFillUnroll;
+  // kv_indices part
+  for (int64_t e0 = begin + threadIdx.x; e0 < min(end, n_idx); e0 += step) {
+    int32_t page[kFillUnroll];
+#pragma unroll
+    for (int u = 0; u < kFillUnroll; ++u) {
+      const int64_t e = e0 + static_cast<int64_t>(u) * blockDim.x;
+      if (e < min(end, n_idx)) {
+        const int i = find_seq(kvp, p.batch, e);
+        const int32_t row = p.table_index ? p.table_index[i] : i;
+        page[u] = p.page_table[static_cast<int64_t>(row) * p.page_table_stride + (e - kvp[i])];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kFillUnroll; ++u) {
+      const int64_t e = e0 + static_cast<int64_t>(u) * blockDim.x;
+      if (e < min(end, n_idx)) {
+        if (p.num_pages > 0 && (page[u] < 0 || page[u] >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
+        p.kv_indices[e] = page[u];
+      }
+    }
+  }
+  // slot_mapping part
+  for (int64_t e0 = max(begin, n_idx) + threadIdx.x; e0 < end; e0 += step) {
+    int64_t slot[kFillUnroll];
+#pragma unroll
+    for (int u = 0; u < kFillUnroll; ++u) {
+      const int64_t t = e0 + static_cast<int64_t>(u) * blockDim.x - n_idx;
+      slot[u] = (t + n_idx < end && t < n_tok) ? token_slot(p, kvp, qop, t) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kFillUnroll; ++u) {
+      const int64_t e = e0 + static_cast<int64_t>(u) * blockDim.x;
+      if (e < end) write_slot(p, e - n_idx, slot[u]);
     }
   }
 }
@@ -247,9 +280,11 @@ __device__ inline void write_seq_outputs(const IndexParams &p, const int32_t *kv
 }
 
 // Split of the fill space [kv_indices | slot_mapping] among blocks, with the
-// capacity checks.
+// capacity and token-count checks.
 __device__ __forceinline__ void fill_block_share(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
                                                  bool report) {
+  if (report && threadIdx.x == 0 && p.expected_tokens >= 0 && qop[p.batch] != p.expected_tokens)
+    raise_deverr(p.error_word, YL_DEVERR_TOKEN_COUNT);
   int64_t n_idx = p.kv_indices ? kvp[p.batch] : 0;
   const int64_t n_slot = p.slot_mapping ? p.slots_cap : 0;
   if (n_idx > p.indices_cap) {

@@ -17,10 +17,14 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "index_device.cuh"
 #include "store_device.cuh"
+#include "tma.cuh"
 
 namespace ylk {
 
@@ -78,20 +82,173 @@ __global__ void __launch_bounds__(kStepThreads, 3) kv_step_kernel(const __grid_c
   }
 }
 
+// TMA-staged fused step.  One CTA per SM owns a contiguous range of rows and
+// stages them in shared memory: at kernel start every staging thread
+// (threads own stage slots t, t + 256, ...) issues bulk loads of its rows, so
+// for a decode step all of the step's K/V reads are in flight from the first
+// microsecond.  While they land, all threads compute the batch scan and this
+// CTA's share of the page arrays; then each staging thread derives its rows'
+// slots, waits for its rows, and bulk-stores them to the pool.
+constexpr int kTmaSlotsPerThread = 8;
+constexpr uint64_t kTmaWaitLimitNs = 2000000000ull;  // 2 s
+constexpr size_t kTmaSmemMax = 232448;               // 227 KB, the B200 per-CTA maximum
+
+static size_t tma_header_bytes(int batch) {
+  const size_t h = kStepThreads * sizeof(uint64_t) + 64 * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t);
+  return (h + 127) & ~static_cast<size_t>(127);
+}
+
+__global__ void __launch_bounds__(kStepThreads, 1)
+    kv_step_tma_kernel(const __grid_constant__ StepParams p, uint32_t row_bytes, uint32_t nslot,
+                       uint32_t rows_per_cta, uint32_t header) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw) + threadIdx.x;
+  int64_t *scratch = reinterpret_cast<int64_t *>(smem_raw + kStepThreads * sizeof(uint64_t));
+  int32_t *kvp = reinterpret_cast<int32_t *>(scratch + 64);
+  int32_t *qop = kvp + (p.ix.batch + 1);
+  char *stage = reinterpret_cast<char *>(smem_raw) + header;
+  const StoreParams &st = p.st;
+  const uint32_t begin = blockIdx.x * rows_per_cta;
+  const uint32_t end = min(begin + rows_per_cta, st.total_rows);
+  const bool report = blockIdx.x == 0;
+  mbar_init(bar, 1);  // each thread waits only on its own barrier
+  fence_mbar_init();
+
+  auto issue = [&](uint32_t r) -> bool {
+    const uint32_t first = begin + r * nslot;
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kStepThreads;
+      if (sl < nslot && first + sl < end) bytes += row_bytes;
+    }
+    if (bytes == 0) return false;
+    mbar_arrive_expect_tx(bar, bytes);
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kStepThreads;
+      if (sl < nslot && first + sl < end) {
+        uint32_t token;
+        const RowAddr a = row_addr(st, first + sl, token);
+        bulk_load(stage + static_cast<size_t>(sl) * row_bytes, a.src, row_bytes, bar);
+      }
+    }
+    return true;
+  };
+
+  uint32_t r = 0, parity = 0;
+  bool have = issue(0);  // the step's K/V reads start now
+
+  if (!scan_batch(p.ix, kvp, qop, scratch, report)) {  // uniform per block
+    if (have) mbar_wait_bounded(bar, parity, kTmaWaitLimitNs);  // let the loads land before leaving
+    return;
+  }
+  const int64_t n_tok = qop[p.ix.batch];
+  if (report && threadIdx.x == 0 && n_tok != p.num_tokens) raise_deverr(p.ix.error_word, YL_DEVERR_TOKEN_COUNT);
+  write_seq_outputs(p.ix, kvp, qop, static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+                    static_cast<int64_t>(gridDim.x) * blockDim.x, true);
+  fill_kv_share(p.ix, kvp, p.num_tokens, report);
+
+  while (have) {
+    const uint32_t first = begin + r * nslot;
+    int64_t slot[kTmaSlotsPerThread];
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kStepThreads;
+      slot[k] = -1;
+      if (sl < nslot && first + sl < end) {
+        const uint32_t row = first + sl;
+        const uint32_t plane = st.by_tokens.div(row);
+        const uint32_t token = row - plane * st.by_tokens.d;
+        if (token < n_tok) slot[k] = token_slot(p.ix, kvp, qop, token);
+        if (plane == 0) write_slot(p.ix, token, slot[k]);  // layer 0's K rows publish the slot mapping
+      }
+    }
+    if (!mbar_wait_bounded(bar, parity, kTmaWaitLimitNs)) {
+      raise_deverr(p.ix.error_word, YL_DEVERR_TIMEOUT);
+      mbar_wait_bounded(bar, parity, kTmaWaitLimitNs);
+      break;
+    }
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kStepThreads;
+      if (sl < nslot && first + sl < end && slot_ok(slot[k], st)) {
+        uint32_t token;
+        const RowAddr a = row_addr(st, first + sl, token);
+        bulk_store(a.dst_base + slot[k] * st.cache_row_stride, stage + static_cast<size_t>(sl) * row_bytes,
+                   row_bytes);
+      }
+    }
+    bulk_commit();
+    ++r;
+    parity ^= 1u;
+    if (begin + r * nslot >= end) break;
+    bulk_wait_read_all();
+    have = issue(r);
+  }
+  bulk_wait_all();
+}
+
 static size_t step_smem(int batch) { return 64 * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t); }
 
-// How yl_kv_step runs: the index build and a PDL-dependent store (default),
-// the one-launch fused kernel (YL_STEP_MODE=fused), or the two launches
-// serialised (YL_STEP_MODE=serial).
-enum class StepMode { kPdl, kFused, kSerial };
+// How yl_kv_step runs (YL_STEP_MODE): the index build and a PDL-dependent
+// store (default, "pdl"), the TMA-staged fused kernel ("tma"), the
+// register-staged fused kernel ("fused"), or the two launches serialised
+// ("serial").  On B200 the PDL form is the fastest measured: the store's
+// first K/V loads overlap the index build without tying up registers or
+// shared memory across it.
+enum class StepMode { kPdl, kTma, kFused, kSerial };
 static StepMode step_mode() {
   static const StepMode m = [] {
     const char *e = std::getenv("YL_STEP_MODE");
     if (e != nullptr && std::strcmp(e, "fused") == 0) return StepMode::kFused;
     if (e != nullptr && std::strcmp(e, "serial") == 0) return StepMode::kSerial;
+    if (e != nullptr && std::strcmp(e, "tma") == 0) return StepMode::kTma;
     return StepMode::kPdl;
   }();
   return m;
+}
+
+static int launch_step_tma(const StepParams &p, int64_t row_bytes, cudaStream_t stream) {
+  static std::mutex mu;
+  static std::vector<char> done;
+  {
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(done.size()) <= dev) done.resize(dev + 1, 0);
+    if (!done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kv_step_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kTmaSmemMax));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kv_step_tma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_last_error(std::string("yl_kv_step: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+        return YL_ERR_CUDA;
+      }
+      done[dev] = 1;
+    }
+  }
+  const size_t header = tma_header_bytes(p.ix.batch);
+  const uint64_t cap = (kTmaSmemMax - header) / static_cast<uint64_t>(row_bytes);
+  const uint64_t max_slots = static_cast<uint64_t>(kStepThreads) * kTmaSlotsPerThread;
+  const uint64_t nslot_cap = cap < max_slots ? cap : max_slots;
+  const uint64_t total = p.st.total_rows;
+  // one CTA per SM, each with enough rows to fill its stage or a fair share
+  uint64_t grid = static_cast<uint64_t>(sm_count());
+  const uint64_t by_rows = (total + 31) / 32;
+  if (by_rows < grid) grid = by_rows;
+  const uint64_t fill = static_cast<uint64_t>(p.ix.indices_cap);
+  const uint64_t by_fill = (fill + 4 * kStepThreads - 1) / (4 * kStepThreads);
+  if (by_fill > grid) grid = by_fill < static_cast<uint64_t>(sm_count()) ? by_fill : sm_count();
+  if (grid < 1) grid = 1;
+  const uint32_t rows_per_cta = static_cast<uint32_t>((total + grid - 1) / grid);
+  const uint32_t nslot = static_cast<uint32_t>(rows_per_cta < nslot_cap ? rows_per_cta : nslot_cap);
+  const size_t smem = header + static_cast<size_t>(nslot) * static_cast<size_t>(row_bytes);
+  kv_step_tma_kernel<<<static_cast<unsigned>(grid), kStepThreads, smem, stream>>>(
+      p, static_cast<uint32_t>(row_bytes), nslot, rows_per_cta, static_cast<uint32_t>(header));
+  return check_launch("yl_kv_step launch");
 }
 
 }  // namespace ylk
@@ -114,6 +271,7 @@ extern "C" int yl_kv_step(const yl_step_args *a, cudaStream_t stream) {
   StorePlan sp;
   rc = prepare_store(&s, true, sp);
   if (rc != YL_OK) return rc;
+  ix.expected_tokens = s.num_tokens;
   if (s.num_tokens == 0) return launch_index(ix, stream);
 
   const int w = fast_vector_bytes();
@@ -127,13 +285,20 @@ extern "C" int yl_kv_step(const yl_step_args *a, cudaStream_t stream) {
     rows = S::R;
   };
   bool fused = ix.batch <= kStepBatchLimit && sp.unit == 16;
+  if (fused && step_mode() == StepMode::kTma && s.row_bytes <= 16384) {
+    StepParams p;
+    p.ix = ix;
+    p.st = sp.p;
+    p.num_tokens = static_cast<uint32_t>(s.num_tokens);
+    return launch_step_tma(p, s.row_bytes, stream);
+  }
   if (fused) {
     bool found = false;
     if (w == 32 && (sp.bits & 31u) == 0) found = dispatch_row_shape(s.row_bytes, 32, pick);
     if (!found) found = dispatch_row_shape(s.row_bytes, 16, pick);
     fused = found;
   }
-  if (!fused || step_mode() != StepMode::kFused) {
+  if (!fused || step_mode() == StepMode::kPdl || step_mode() == StepMode::kSerial) {
     // Two launches: the index build, then the store reading its slot mapping.
     // In PDL mode the store is the index kernel's programmatic dependent: its
     // K/V loads overlap the index build and only the slot reads wait for it.

@@ -26,9 +26,11 @@
 #include <mutex>
 #include <tuple>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "store_device.cuh"
+#include "tma.cuh"
 
 namespace ylk {
 
@@ -55,6 +57,94 @@ __global__ void __launch_bounds__(256) store_rows_kernel(const __grid_constant__
     base += num_groups * R;
     if (base < p.total_rows) b.load(p, base, lane);
   }
+}
+
+// TMA path: one CTA per SM stages its rows in shared memory.  The CTA owns a
+// contiguous range of rows; a round loads up to nslot of them with bulk
+// copies (thread t owns stage slots t, t + 256, ...), so at kernel start
+// nearly all of a decode step's K/V reads are in flight before the kernel
+// waits for its slots (pdl_wait, when launched behind the index build).  Once
+// a thread's rows have landed and their slots are known it bulk-stores them
+// from shared memory and, when the next round needs its stage slots, waits
+// only until those stores have read shared memory.
+constexpr int kTmaThreads = 256;
+constexpr int kTmaSlotsPerThread = 8;
+constexpr uint64_t kTmaWaitLimitNs = 2000000000ull;  // 2 s
+constexpr size_t kTmaBarrierBytes = kTmaThreads * sizeof(uint64_t);
+
+template <typename SlotT>
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    store_rows_tma_kernel(const __grid_constant__ StoreParams p, uint32_t row_bytes, uint32_t nslot,
+                          uint32_t rows_per_cta) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw) + threadIdx.x;
+  char *stage = reinterpret_cast<char *>(smem_raw) + kTmaBarrierBytes;
+  const uint32_t begin = blockIdx.x * rows_per_cta;
+  const uint32_t end = min(begin + rows_per_cta, p.total_rows);
+  mbar_init(bar, 1);  // each thread waits only on its own barrier
+  fence_mbar_init();
+
+  // Issue round r's loads; false when this thread has no row in it.
+  auto issue = [&](uint32_t r) -> bool {
+    const uint32_t first = begin + r * nslot;
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kTmaThreads;
+      if (sl < nslot && first + sl < end) bytes += row_bytes;
+    }
+    if (bytes == 0) return false;
+    mbar_arrive_expect_tx(bar, bytes);
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kTmaThreads;
+      if (sl < nslot && first + sl < end) {
+        uint32_t token;
+        const RowAddr a = row_addr(p, first + sl, token);
+        bulk_load(stage + static_cast<size_t>(sl) * row_bytes, a.src, row_bytes, bar);
+      }
+    }
+    return true;
+  };
+
+  uint32_t r = 0, parity = 0;
+  bool have = issue(0);
+  pdl_wait();  // slots may come from the kernel this one was launched behind
+  while (have) {
+    const uint32_t first = begin + r * nslot;
+    int64_t slot[kTmaSlotsPerThread];
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kTmaThreads;
+      slot[k] = -1;
+      if (sl < nslot && first + sl < end) {
+        const uint32_t plane = p.by_tokens.div(first + sl);
+        slot[k] = load_slot<SlotT>(p.slots, first + sl - plane * p.by_tokens.d);
+      }
+    }
+    if (!mbar_wait_bounded(bar, parity, kTmaWaitLimitNs)) {
+      raise_deverr(p.error_word, YL_DEVERR_TIMEOUT);
+      mbar_wait_bounded(bar, parity, kTmaWaitLimitNs);  // let this thread's loads land before leaving
+      break;
+    }
+#pragma unroll
+    for (int k = 0; k < kTmaSlotsPerThread; ++k) {
+      const uint32_t sl = threadIdx.x + k * kTmaThreads;
+      if (sl < nslot && first + sl < end && slot_ok(slot[k], p)) {
+        uint32_t token;
+        const RowAddr a = row_addr(p, first + sl, token);
+        bulk_store(a.dst_base + slot[k] * p.cache_row_stride, stage + static_cast<size_t>(sl) * row_bytes,
+                   row_bytes);
+      }
+    }
+    bulk_commit();
+    ++r;
+    parity ^= 1u;
+    if (begin + r * nslot >= end) break;
+    bulk_wait_read_all();  // this thread's stage slots are free again
+    have = issue(r);
+  }
+  bulk_wait_all();
 }
 
 // Generic path: any row size and alignment, unit U in {1, 2, 4, 8, 16} bytes,
@@ -103,7 +193,7 @@ struct StoreVariant {
 int fast_vector_bytes() {
   static int w = [] {
     const char *e = std::getenv("YL_STORE_VECTOR_BYTES");
-    return (e != nullptr && std::strcmp(e, "32") == 0) ? 32 : 16;
+    return (e != nullptr && std::strcmp(e, "16") == 0) ? 16 : 32;
   }();
   return w;
 }
@@ -206,7 +296,75 @@ int prepare_store(const yl_store_args *a, bool need_slots, StorePlan &plan) {
   return YL_OK;
 }
 
+// Store engine: register-staged vector copies (default) or TMA bulk copies
+// staged in shared memory (YL_STORE_ENGINE=tma).
+static bool use_tma_engine() {
+  static const bool t = [] {
+    const char *e = std::getenv("YL_STORE_ENGINE");
+    return e != nullptr && std::strcmp(e, "tma") == 0;
+  }();
+  return t;
+}
+
+// Staging per CTA: 200 KB of the SM's 228 KB, leaving room for two index-build
+// blocks to stay resident beside it when the store runs as their PDL dependent.
+constexpr size_t kTmaMaxSmem = 200 * 1024;
+
+static int launch_store_tma(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStream_t stream, bool pdl) {
+  using TmaKernel = void (*)(StoreParams, uint32_t, uint32_t, uint32_t);
+  const TmaKernel fn = slot64 ? store_rows_tma_kernel<int64_t> : store_rows_tma_kernel<int32_t>;
+  static std::mutex mu;
+  static std::vector<char> done;
+  {
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(done.size()) <= dev) done.resize(dev + 1, 0);
+    if (!(done[dev] & (slot64 ? 2 : 1))) {
+      cudaError_t e =
+          cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTmaMaxSmem));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_last_error(std::string("yl_kv_store: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+        return YL_ERR_CUDA;
+      }
+      done[dev] |= (slot64 ? 2 : 1);
+    }
+  }
+  const uint64_t cap_slots = (kTmaMaxSmem - kTmaBarrierBytes) / static_cast<uint64_t>(row_bytes);
+  const uint32_t nslot = static_cast<uint32_t>(
+      cap_slots < static_cast<uint64_t>(kTmaThreads * kTmaSlotsPerThread) ? cap_slots : kTmaThreads * kTmaSlotsPerThread);
+  const uint64_t total = plan.p.total_rows;
+  uint64_t grid = (total + 63) / 64;
+  const uint64_t sms = static_cast<uint64_t>(sm_count());
+  if (grid > sms) grid = sms;
+  if (grid < 1) grid = 1;
+  const uint32_t rows_per_cta = static_cast<uint32_t>((total + grid - 1) / grid);
+  const uint64_t per_round = rows_per_cta < nslot ? rows_per_cta : nslot;
+  const size_t smem = kTmaBarrierBytes + static_cast<size_t>(per_round) * static_cast<size_t>(row_bytes);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kTmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, plan.p, static_cast<uint32_t>(row_bytes),
+                                           static_cast<uint32_t>(per_round), rows_per_cta);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error(std::string("yl_kv_store launch: ") + cudaGetErrorString(e));
+    return YL_ERR_CUDA;
+  }
+  return check_launch("yl_kv_store launch");
+}
+
 int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStream_t stream, bool pdl) {
+  if (use_tma_engine() && plan.unit == 16 && row_bytes <= 16384) return launch_store_tma(plan, row_bytes, slot64, stream, pdl);
   StoreVariant var{};
   bool fast = false;
   const int w = fast_vector_bytes();

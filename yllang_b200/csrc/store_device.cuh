@@ -186,8 +186,9 @@ inline bool dispatch_row_shape(int64_t row_bytes, int w, F &&f) {
   }
 }
 
-// Vector width of the fast path: 16-byte vectors by default, 32-byte (v8)
-// vectors when YL_STORE_VECTOR_BYTES=32 is set in the environment.
+// Vector width of the fast path: 32-byte vectors (ld/st .v8.b32, sm_100) when
+// every address and stride is 32-byte aligned, else 16-byte vectors;
+// YL_STORE_VECTOR_BYTES=16 forces 16-byte vectors.
 int fast_vector_bytes();
 
 // Host halves of the entry points (kv_store.cu, index_build.cu), shared with
