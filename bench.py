@@ -41,11 +41,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 import yllang_b200 as yl  # noqa: E402
-from yllang_b200 import workloads  # noqa: E402
+from yllang_b200 import sharding, workloads  # noqa: E402
 
 METRIC = "KV-store GB/s (% of HBM peak) + tokens/s stored; index-build µs/batch"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one all-layer store launch of the single-GPU
+# Llama-3-8B decode step, from one ncu capture of store_rows_kernel at that
+# launch shape: 33,565,440 read + 1,564,928 written (the rows' writes stay in
+# L2 during the launch and are written back after it).
+STORE_TRAFFIC_NCU = {("llama3_decode", 1): 35130368}
 
 
 # ---------------------------------------------------------------------------
@@ -74,21 +79,11 @@ def barrier(world):
 
 
 def reduce_max(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return sharding.max_over_ranks(x) if world > 1 else x
 
 
 def reduce_sum(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return sharding.sum_over_ranks(x) if world > 1 else x
 
 
 # ---------------------------------------------------------------------------
@@ -153,7 +148,8 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 def make_batches(name: str, world: int, pool_bytes: int, rotate: int):
     """R batches of one workload for this rank (same lengths, different pages)."""
-    heads = 8 // world
+    h0, h1 = sharding.head_range(0, world, 8)  # raises unless the 8 KV heads split evenly
+    heads = h1 - h0
     if name == "llama3_decode":
         layers, ps, row = 32, 16, heads * 128 * 2
         P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
@@ -491,8 +487,10 @@ def run_ours(args, world, rank, local):
         layer) for layer in range(L)], min(K, 16)) / L
     assert int(err.item()) == 0, f"device error word {int(err.item()):#x}"
 
+    # every collective runs on all ranks, in the same order, before rank 0 reports
     per_step_s = ms_max / 1e3 / K
     total_store = reduce_sum(float(store_bytes), world)
+    total_step = reduce_sum(float(step_bytes), world)
     value = total_store / per_step_s / 1e9
     tokens_global = b0.tokens  # every rank stores its head slice of every token
     peak, peak_kind = load_peaks()
@@ -520,7 +518,7 @@ def run_ours(args, world, rank, local):
         "pct_hbm": round(100 * value / (peak * world), 2),
         "index_build_us": round(index_us, 3),
         "step_us": round(ms_max * 1e3 / K, 3),
-        "step_gbs": round(reduce_sum(float(step_bytes), world) / per_step_s / 1e9, 1),
+        "step_gbs": round(total_step / per_step_s / 1e9, 1),
         "store_us": round(store_us, 3),
         "store_gbs": round(achieved, 1),
         "index_gbs": round(index_bytes / (index_us * 1e-6) / 1e9, 1),
@@ -528,7 +526,9 @@ def run_ours(args, world, rank, local):
                             "gbs": round(store_bytes / L / (layer_us * 1e-6) / 1e9, 1)},
         "roofline": {"bound": "hbm", "kernel": "store_rows_kernel (all layers of a step, one launch)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": args.traffic,
+                     "frac": round(achieved / peak, 4),
+                     "traffic": args.traffic if args.traffic is not None else STORE_TRAFFIC_NCU.get(
+                         (args.workload, world)),
                      "peak_source": f"{peak_kind} hbm_gbs (copy)", "algorithmic_bytes_per_launch": store_bytes,
                      "launch_us": round(store_us, 3),
                      "timing": f"{n_sep} back-to-back launches in one CUDA graph, events around the replays"},
