@@ -32,15 +32,18 @@
 
 namespace ylk {
 
-constexpr int kIndexThreads = 256;    // single-launch and fill kernels
-constexpr int kScanThreads = 1024;    // one-block scan of the two-launch form
+constexpr int kIndexThreads = 256;     // small batches: many blocks, cheap redundant scans
+constexpr int kIndexThreadsBig = 1024; // batches above kBigBatch: 4x fewer blocks repeat the scan
+constexpr int kBigBatch = 1024;
+constexpr int kScanThreads = 1024;     // one-block scan of the two-launch form
 constexpr int kSmemBatchLimit = 16384;
 
 // Single-launch form (B <= kSmemBatchLimit).
-__global__ void __launch_bounds__(kIndexThreads) build_index_kernel(const __grid_constant__ IndexParams p) {
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) build_index_kernel(const __grid_constant__ IndexParams p) {
   extern __shared__ int64_t smem[];
-  int64_t *scratch = smem;                                   // 64 x int64
-  int32_t *kvp = reinterpret_cast<int32_t *>(smem + 64);     // [B+1]
+  int64_t *scratch = smem;                                   // kScanScratch x int64
+  int32_t *kvp = reinterpret_cast<int32_t *>(smem + kScanScratch);  // [B+1]
   int32_t *qop = kvp + (p.batch + 1);                        // [B+1]
   const bool report = blockIdx.x == 0;
   pdl_trigger();  // a store launched as our dependent may start loading its K/V rows now
@@ -53,7 +56,7 @@ __global__ void __launch_bounds__(kIndexThreads) build_index_kernel(const __grid
 // Two-launch form, launch 1 (one block): scan straight into the outputs.  On
 // overflow kv_indptr[B] is set to -1 so that launch 2 skips the fill.
 __global__ void __launch_bounds__(kScanThreads) scan_index_kernel(const __grid_constant__ IndexParams p) {
-  __shared__ int64_t scratch[64];
+  __shared__ int64_t scratch[kScanScratch];
   if (!scan_batch(p, p.kv_indptr, p.qo_indptr, scratch, true)) {
     if (threadIdx.x == 0) p.kv_indptr[p.batch] = -1;
     return;
@@ -62,13 +65,13 @@ __global__ void __launch_bounds__(kScanThreads) scan_index_kernel(const __grid_c
 }
 
 // Two-launch form, launch 2: fill from the scanned outputs.
-__global__ void __launch_bounds__(kIndexThreads) fill_index_kernel(const __grid_constant__ IndexParams p) {
+__global__ void __launch_bounds__(kIndexThreadsBig) fill_index_kernel(const __grid_constant__ IndexParams p) {
   pdl_trigger();
   if (p.kv_indptr[p.batch] < 0) return;
   fill_block_share(p, p.kv_indptr, p.qo_indptr, blockIdx.x == 0);
 }
 
-static size_t single_launch_smem(int batch) { return 64 * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t); }
+static size_t single_launch_smem(int batch) { return kScanScratch * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t); }
 
 // Opt the single-launch kernel into > 48 KB dynamic shared memory once per device.
 static int ensure_smem_attr() {
@@ -81,8 +84,12 @@ static int ensure_smem_attr() {
     // No carveout preference: the store kernel that runs as this kernel's PDL
     // dependent takes the default split too, so both fit on one SM at once (a
     // differing preference keeps the store's blocks off an SM until it drains).
-    const cudaError_t e = cudaFuncSetAttribute(build_index_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(single_launch_smem(kSmemBatchLimit)));
+    cudaError_t e = cudaFuncSetAttribute(build_index_kernel<kIndexThreads>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(single_launch_smem(kSmemBatchLimit)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(build_index_kernel<kIndexThreadsBig>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(single_launch_smem(kSmemBatchLimit)));
     if (e != cudaSuccess) {
       set_last_error(std::string("yl_build_index: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
       return YL_ERR_CUDA;
@@ -118,6 +125,9 @@ int prepare_index(const yl_index_args *a, IndexParams &p) {
                 a->batch_size);
   if (a->page_table_stride < 0)
     return fail(YL_ERR_BAD_SIZE, "yl_build_index: page_table_stride=%lld < 0", a->page_table_stride);
+  if ((a->kv_indices ? a->kv_indices_capacity : 0) + (a->slot_mapping ? a->slot_capacity : 0) >= (1ll << 31))
+    return fail(YL_ERR_UNSUPPORTED, "yl_build_index: kv_indices + slot capacity of %lld elements reaches 2^31",
+                (a->kv_indices ? a->kv_indices_capacity : 0) + (a->slot_mapping ? a->slot_capacity : 0));
   if (a->slot_mapping && (reinterpret_cast<uintptr_t>(a->slot_mapping) & (a->slot_is_int64 ? 7u : 3u)))
     return fail(YL_ERR_ALIGNMENT, "yl_build_index: slot_mapping is not aligned to its element size");
 
@@ -147,26 +157,30 @@ int prepare_index(const yl_index_args *a, IndexParams &p) {
 }
 
 int launch_index(const IndexParams &p, cudaStream_t stream) {
-  // Blocks: one fill element per thread for small batches (each block scans
-  // the whole batch, so big batches get fewer, busier blocks).
+  // Blocks: one fill element per thread; each block scans the whole batch,
+  // so big batches use 1024-thread blocks (4x fewer scans), at most one per SM.
   const int64_t work = p.indices_cap + p.slots_cap;
   const int64_t sms = sm_count();
-  const int64_t per_block = p.batch <= 2048 ? kIndexThreads : 4 * kIndexThreads;
-  const int64_t cap = p.batch <= 2048 ? 4 * sms : sms;
-  int64_t blocks = (work + per_block - 1) / per_block;
+  const bool big = p.batch > kBigBatch;
+  const int threads = big ? kIndexThreadsBig : kIndexThreads;
+  const int64_t cap = big ? sms : 4 * sms;
+  int64_t blocks = (work + threads - 1) / threads;
   if (blocks < 1) blocks = 1;
   if (blocks > cap) blocks = cap;
 
   if (p.batch <= kSmemBatchLimit) {
     const int rc = ensure_smem_attr();
     if (rc != YL_OK) return rc;
-    build_index_kernel<<<static_cast<unsigned>(blocks), kIndexThreads, single_launch_smem(p.batch), stream>>>(p);
+    if (big)
+      build_index_kernel<kIndexThreadsBig><<<static_cast<unsigned>(blocks), kIndexThreadsBig, single_launch_smem(p.batch), stream>>>(p);
+    else
+      build_index_kernel<kIndexThreads><<<static_cast<unsigned>(blocks), kIndexThreads, single_launch_smem(p.batch), stream>>>(p);
     return check_launch("yl_build_index launch");
   }
   scan_index_kernel<<<1, kScanThreads, 0, stream>>>(p);
   int rc = check_launch("yl_build_index scan launch");
   if (rc != YL_OK) return rc;
-  fill_index_kernel<<<static_cast<unsigned>(blocks), kIndexThreads, 0, stream>>>(p);
+  fill_index_kernel<<<static_cast<unsigned>(blocks), kIndexThreadsBig, 0, stream>>>(p);
   return check_launch("yl_build_index fill launch");
 }
 

@@ -39,6 +39,9 @@ struct IndexParams {
   int64_t expected_tokens;  // step only: the store's N, checked against the sum of new_len (-1: no check)
 };
 
+// int64 words of shared scratch the scan needs: 2 x 32 warp totals + 2 block totals.
+constexpr int kScanScratch = 66;
+
 struct SeqFacts {
   int32_t prior;  // clamped to >= 0
   int32_t fresh;  // new tokens, clamped to >= 0
@@ -82,58 +85,12 @@ __device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool 
   return f;
 }
 
-// Exclusive block scan of two int64 values per thread.  `scratch` holds 64
-// int64; returns the block totals through ta/tb.  Ends synchronised.
-__device__ __forceinline__ void block_scan2(int64_t &a, int64_t &b, int64_t &ta, int64_t &tb, int64_t *scratch) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
-  const int64_t a0 = a, b0 = b;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int64_t xa = __shfl_up_sync(0xffffffffu, a, o);
-    const int64_t xb = __shfl_up_sync(0xffffffffu, b, o);
-    if (lane >= o) {
-      a += xa;
-      b += xb;
-    }
-  }
-  if (lane == 31) {
-    scratch[warp] = a;
-    scratch[32 + warp] = b;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int64_t x = lane < nwarps ? scratch[lane] : 0;
-    int64_t y = lane < nwarps ? scratch[32 + lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t xx = __shfl_up_sync(0xffffffffu, x, o);
-      const int64_t yy = __shfl_up_sync(0xffffffffu, y, o);
-      if (lane >= o) {
-        x += xx;
-        y += yy;
-      }
-    }
-    scratch[lane] = x;
-    scratch[32 + lane] = y;
-  }
-  __syncthreads();
-  const int64_t pa = warp > 0 ? scratch[warp - 1] : 0;
-  const int64_t pb = warp > 0 ? scratch[32 + warp - 1] : 0;
-  ta = scratch[nwarps - 1];
-  tb = scratch[32 + nwarps - 1];
-  a = pa + a - a0;
-  b = pb + b - b0;
-  __syncthreads();
-}
-
 // Phase A: scan page and token counts of all sequences into kvp[0..B] and
 // qop[0..B] (shared or global memory).  The counts are first staged in
-// kvp/qop (coalesced), then every thread scans a contiguous chunk of them
-// serially and one block scan of the chunk totals gives the chunk offsets.
-// Returns false (uniformly across the block) when a sum passes INT32_MAX; the
-// fill must then be skipped.
+// kvp/qop (coalesced); each warp then scans its contiguous segment 32 entries
+// at a time with shuffles (conflict-free), the warp totals are scanned once,
+// and each warp adds its offset.  Returns false (uniformly across the block)
+// when a sum passes INT32_MAX; the fill must then be skipped.
 __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *qop, int64_t *scratch, bool report) {
   const int B = p.batch;
   for (int i = threadIdx.x; i < B; i += blockDim.x) {
@@ -142,26 +99,68 @@ __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *q
     qop[i] = f.fresh;
   }
   __syncthreads();
-  const int per = (B + blockDim.x - 1) / blockDim.x;
-  const int lo = min(B, static_cast<int>(threadIdx.x) * per);
-  const int hi = min(B, lo + per);
-  int64_t a = 0, b = 0;
-  for (int i = lo; i < hi; ++i) {
-    a += kvp[i];
-    b += qop[i];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int seg = (((B + nwarps - 1) / nwarps) + 31) & ~31;
+  const int s0 = min(B, warp * seg), s1 = min(B, s0 + seg);
+  int64_t ca = 0, cb = 0;  // running totals of this warp's segment
+  for (int base = s0; base < s1; base += 32) {
+    const int i = base + lane;
+    const int64_t x = i < s1 ? kvp[i] : 0, y = i < s1 ? qop[i] : 0;
+    int64_t a = x, b = y;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t ua = __shfl_up_sync(0xffffffffu, a, o);
+      const int64_t ub = __shfl_up_sync(0xffffffffu, b, o);
+      if (lane >= o) {
+        a += ua;
+        b += ub;
+      }
+    }
+    // exclusive within the segment; int32 wrap here is harmless, the totals
+    // are checked below before any offset is used
+    if (i < s1) {
+      kvp[i] = static_cast<int32_t>(ca + a - x);
+      qop[i] = static_cast<int32_t>(cb + b - y);
+    }
+    ca += __shfl_sync(0xffffffffu, a, 31);
+    cb += __shfl_sync(0xffffffffu, b, 31);
   }
-  int64_t ta, tb;
-  block_scan2(a, b, ta, tb, scratch);  // ends synchronised: every count has been read
+  if (lane == 0) {
+    scratch[warp] = ca;
+    scratch[32 + warp] = cb;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int64_t a = lane < nwarps ? scratch[lane] : 0, b = lane < nwarps ? scratch[32 + lane] : 0;
+    const int64_t a0 = a, b0 = b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t ua = __shfl_up_sync(0xffffffffu, a, o);
+      const int64_t ub = __shfl_up_sync(0xffffffffu, b, o);
+      if (lane >= o) {
+        a += ua;
+        b += ub;
+      }
+    }
+    scratch[lane] = a - a0;  // exclusive warp offsets
+    scratch[32 + lane] = b - b0;
+    if (lane == 31) {
+      scratch[64] = a;  // block totals
+      scratch[65] = b;
+    }
+  }
+  __syncthreads();
+  const int64_t ta = scratch[64], tb = scratch[65];
   if (ta > INT_MAX || tb > INT_MAX) {
     if (report && threadIdx.x == 0) raise_deverr(p.error_word, YL_DEVERR_INDPTR_OVERFLOW);
     return false;
   }
-  for (int i = lo; i < hi; ++i) {
-    const int32_t x = kvp[i], y = qop[i];
-    kvp[i] = static_cast<int32_t>(a);
-    qop[i] = static_cast<int32_t>(b);
-    a += x;
-    b += y;
+  const int32_t oa = static_cast<int32_t>(scratch[warp]), ob = static_cast<int32_t>(scratch[32 + warp]);
+  for (int i = s0 + lane; i < s1; i += 32) {
+    kvp[i] += oa;
+    qop[i] += ob;
   }
   if (threadIdx.x == 0) {
     kvp[B] = static_cast<int32_t>(ta);
@@ -171,15 +170,32 @@ __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *q
   return true;
 }
 
-// Largest i in [0, n) with off[i] <= e, given off[0] <= e < off[n].
-__device__ __forceinline__ int find_seq(const int32_t *off, int n, int64_t e) {
-  int lo = 0, hi = n;
+// Largest i in [0, n] with off[i] <= e, given off[0] <= e < off[n], by a
+// branchless walk down a power-of-two ladder (`top` = the largest power of
+// two <= n, or 0 when n == 0); 32-bit, for the fill loops.
+__device__ __forceinline__ int find_seq32(const int32_t *off, int n, int32_t e, int top) {
+  int lo = 0;
+  for (int step = top; step > 0; step >>= 1) {
+    const int c = lo + step;
+    if (c <= n && off[c] <= e) lo = c;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ int pow2_floor(int n) { return n > 0 ? 1 << (31 - __clz(n)) : 0; }
+
+// Largest i in [lo, hi) with off[i] <= e, given off[lo] <= e < off[hi].
+__device__ __forceinline__ int find_seq_in(const int32_t *off, int lo, int hi, int64_t e) {
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (off[mid] <= e) lo = mid; else hi = mid;
   }
   return lo;
 }
+
+// Largest i in [0, n) with off[i] <= e, given off[0] <= e < off[n].
+__device__ __forceinline__ int find_seq(const int32_t *off, int n, int64_t e) { return find_seq_in(off, 0, n, e); }
+
 
 __device__ __forceinline__ void write_slot(const IndexParams &p, int64_t t, int64_t slot) {
   if (p.slot64) static_cast<int64_t *>(p.slot_mapping)[t] = slot;
@@ -196,18 +212,15 @@ __device__ __forceinline__ void kv_index_elem(const IndexParams &p, const int32_
   p.kv_indices[e] = page;
 }
 
-// Slot of new token t < qo_indptr[B], or -1 when it has none (its position
+// Slot of position `pos` of sequence i, or -1 when it has none (the position
 // is past the sequence's page-table row, or its page is not a pool page).
-__device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
-                                              int64_t t) {
-  const int i = find_seq(qop, p.batch, t);
-  const int64_t pos = static_cast<int64_t>(max(p.prior_len[i], 0)) + (t - qop[i]);
+__device__ __forceinline__ int64_t slot_at(const IndexParams &p, const int32_t *kvp, int i, int64_t pos) {
   const int32_t pages = kvp[i + 1] - kvp[i];
-  if (pos >= (1ll << 31)) return -1;
+  if (pos < 0 || pos >= (1ll << 31)) return -1;
   const uint32_t pidx = p.by_page.div(static_cast<uint32_t>(pos));
   if (static_cast<int64_t>(pidx) >= pages) return -1;
-  const int32_t row = p.table_index ? p.table_index[i] : i;
-  const int32_t page = p.page_table[static_cast<int64_t>(row) * p.page_table_stride + pidx];
+  const int32_t row = p.table_index ? __ldg(p.table_index + i) : i;
+  const int32_t page = __ldg(p.page_table + static_cast<int64_t>(row) * p.page_table_stride + pidx);
   const bool in_range = page >= 0 && (p.num_pages <= 0 || page < p.num_pages);
   const int64_t s = static_cast<int64_t>(page) * p.page_size + (pos - static_cast<int64_t>(pidx) * p.page_size);
   if (in_range && (p.slot64 || s <= INT_MAX)) return s;
@@ -215,51 +228,45 @@ __device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_
   return -1;
 }
 
-// Phase C for the elements [begin, end) of [kv_indices | slot_mapping].  Slot
-// entries past qo_indptr[B] (up to the slot capacity) are written as -1.
-// Each thread gathers kFillUnroll elements per pass with independent chains
-// (search, page-table read), so their global reads are in flight together.
-// Each element belongs to exactly one block, so every block reports its own.
-constexpr int kFillUnroll = 4;
+// Slot of new token t < qo_indptr[B] (the token's sequence found by search).
+__device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
+                                              int64_t t) {
+  const int i = find_seq(qop, p.batch, t);
+  return slot_at(p, kvp, i, static_cast<int64_t>(max(p.prior_len[i], 0)) + (t - qop[i]));
+}
 
-__device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, const int32_t *qop, int64_t n_idx,
-                                  int64_t begin, int64_t end) {
-  const int64_t n_tok = qop[p.batch];
-  const int64_t step = static_cast<int64_t>(blockDim.x) * kFillUnroll;
-  // kv_indices part
-  for (int64_t e0 = begin + threadIdx.x; e0 < min(end, n_idx); e0 += step) {
-    int32_t page[kFillUnroll];
-#pragma unroll
-    for (int u = 0; u < kFillUnroll; ++u) {
-      const int64_t e = e0 + static_cast<int64_t>(u) * blockDim.x;
-      if (e < min(end, n_idx)) {
-        const int i = find_seq(kvp, p.batch, e);
-        const int32_t row = p.table_index ? p.table_index[i] : i;
-        page[u] = p.page_table[static_cast<int64_t>(row) * p.page_table_stride + (e - kvp[i])];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kFillUnroll; ++u) {
-      const int64_t e = e0 + static_cast<int64_t>(u) * blockDim.x;
-      if (e < min(end, n_idx)) {
-        if (p.num_pages > 0 && (page[u] < 0 || page[u] >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
-        p.kv_indices[e] = page[u];
-      }
-    }
+// Phase C for the elements [begin, end) of [kv_indices | slot_mapping]: one
+// element per thread per pass, its sequence found by a branchless search over
+// the scanned offsets, gathered from that sequence's page-table row
+// (coalesced row reads and output writes).  The whole fill space is below
+// 2^31 elements (checked on the host), so element arithmetic is 32-bit.
+// Slot entries past qo_indptr[B] (up to the slot capacity) are written as -1.
+// Each element belongs to exactly one block, so every block reports its own.
+// Measured on B200 and slower: warp-cooperative searches (two per chunk,
+// then a per-lane search of the chunk's span), multi-element unrolled passes,
+// and per-block walks over the spanned sequences (the decode batch is
+// latency-bound at one element per thread; any serial per-block search lands
+// on its critical path).
+__device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, const int32_t *qop, int32_t n_idx,
+                                  int32_t begin, int32_t end) {
+  const int32_t n_tok = qop[p.batch];
+  const int top = pow2_floor(p.batch);
+  const int32_t kv_end = min(end, n_idx);
+  for (int32_t e = begin + static_cast<int32_t>(threadIdx.x); e < kv_end; e += blockDim.x) {
+    const int i = find_seq32(kvp, p.batch, e, top);
+    const int32_t row = p.table_index ? __ldg(p.table_index + i) : i;
+    const int32_t page = __ldg(p.page_table + static_cast<int64_t>(row) * p.page_table_stride + (e - kvp[i]));
+    if (p.num_pages > 0 && (page < 0 || page >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
+    p.kv_indices[e] = page;
   }
-  // slot_mapping part
-  for (int64_t e0 = max(begin, n_idx) + threadIdx.x; e0 < end; e0 += step) {
-    int64_t slot[kFillUnroll];
-#pragma unroll
-    for (int u = 0; u < kFillUnroll; ++u) {
-      const int64_t t = e0 + static_cast<int64_t>(u) * blockDim.x - n_idx;
-      slot[u] = (t + n_idx < end && t < n_tok) ? token_slot(p, kvp, qop, t) : -1;
+  for (int32_t e = max(begin, n_idx) + static_cast<int32_t>(threadIdx.x); e < end; e += blockDim.x) {
+    const int32_t t = e - n_idx;
+    int64_t slot = -1;
+    if (t < n_tok) {
+      const int i = find_seq32(qop, p.batch, t, top);
+      slot = slot_at(p, kvp, i, static_cast<int64_t>(max(__ldg(p.prior_len + i), 0)) + (t - qop[i]));
     }
-#pragma unroll
-    for (int u = 0; u < kFillUnroll; ++u) {
-      const int64_t e = e0 + static_cast<int64_t>(u) * blockDim.x;
-      if (e < end) write_slot(p, e - n_idx, slot[u]);
-    }
+    write_slot(p, t, slot);
   }
 }
 
@@ -293,11 +300,12 @@ __device__ __forceinline__ void fill_block_share(const IndexParams &p, const int
   }
   if (p.slot_mapping && qop[p.batch] > p.slots_cap && report && threadIdx.x == 0)
     raise_deverr(p.error_word, YL_DEVERR_SLOTS_CAP);
-  const int64_t work = n_idx + n_slot;
+  const int64_t work = n_idx + n_slot;  // < 2^31 (checked on the host)
   const int64_t chunk = (work + gridDim.x - 1) / gridDim.x;
   const int64_t begin = static_cast<int64_t>(blockIdx.x) * chunk;
   const int64_t end = min(begin + chunk, work);
-  if (begin < end) fill_range(p, kvp, qop, n_idx, begin, end);
+  if (begin < end)
+    fill_range(p, kvp, qop, static_cast<int32_t>(n_idx), static_cast<int32_t>(begin), static_cast<int32_t>(end));
 }
 
 // kv_indices share of this block when the slots of tokens [0, slot_begin) are

@@ -45,8 +45,8 @@ int blocks_per_sm(const void *fn, size_t smem);  // kv_store.cu, at 256 threads
 template <int W, int G, int VPL, int R>
 __global__ void __launch_bounds__(kStepThreads, 3) kv_step_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ int64_t smem[];
-  int64_t *scratch = smem;                                // 64 x int64
-  int32_t *kvp = reinterpret_cast<int32_t *>(smem + 64);  // [B+1]
+  int64_t *scratch = smem;                                // kScanScratch x int64
+  int32_t *kvp = reinterpret_cast<int32_t *>(smem + kScanScratch);  // [B+1]
   int32_t *qop = kvp + (p.ix.batch + 1);                  // [B+1]
   const uint32_t lane = threadIdx.x % G;
   const uint32_t group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
@@ -94,7 +94,7 @@ constexpr uint64_t kTmaWaitLimitNs = 2000000000ull;  // 2 s
 constexpr size_t kTmaSmemMax = 232448;               // 227 KB, the B200 per-CTA maximum
 
 static size_t tma_header_bytes(int batch) {
-  const size_t h = kStepThreads * sizeof(uint64_t) + 64 * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t);
+  const size_t h = kStepThreads * sizeof(uint64_t) + kScanScratch * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t);
   return (h + 127) & ~static_cast<size_t>(127);
 }
 
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw) + threadIdx.x;
   int64_t *scratch = reinterpret_cast<int64_t *>(smem_raw + kStepThreads * sizeof(uint64_t));
-  int32_t *kvp = reinterpret_cast<int32_t *>(scratch + 64);
+  int32_t *kvp = reinterpret_cast<int32_t *>(scratch + kScanScratch);
   int32_t *qop = kvp + (p.ix.batch + 1);
   char *stage = reinterpret_cast<char *>(smem_raw) + header;
   const StoreParams &st = p.st;
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   bulk_wait_all();
 }
 
-static size_t step_smem(int batch) { return 64 * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t); }
+static size_t step_smem(int batch) { return kScanScratch * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t); }
 
 // How yl_kv_step runs (YL_STEP_MODE): the index build and a PDL-dependent
 // store (default, "pdl"), the TMA-staged fused kernel ("tma"), the
