@@ -537,9 +537,35 @@ def run_ours(args, world, rank, local):
     }
     if e2e is not None:
         line["e2e"] = e2e
+    if not args.no_gather:
+        line["embedding_gather"] = bench_gather(dev, peak)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_store_step_sample(b0, seconds=args.cpu_seconds)
     print(json.dumps(line), flush=True)
+
+
+def bench_gather(dev, peak: float, tokens: int = 4096, sets: int = 32) -> dict:
+    """The embedding lookup on the store's copy engine: Qwen3-0.6B's token
+    table (151936 x 1024 bf16, 311 MB > L2), `tokens` uniformly drawn ids per
+    launch, ids and outputs rotating over `sets` sets.  Algorithmic bytes per
+    launch: ids + the gathered rows read + the output rows written."""
+    V, E = 151936, 1024
+    table = torch.randn(V, E, device=dev, dtype=torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(7)
+    ids = [torch.randint(0, V, (tokens,), generator=g, device=dev, dtype=torch.int32) for _ in range(sets)]
+    outs = [torch.empty(tokens, E, dtype=torch.bfloat16, device=dev) for _ in range(sets)]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for r in range(sets):
+        yl.gather_rows(ids[r], table, out=outs[r], error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(outs[0], table[ids[0].long()])
+    us = per_launch_us(sets, lambda r: [lambda: yl.gather_rows(ids[r], table, out=outs[r], error_word=err)], 256)
+    nbytes = tokens * 4 + 2 * tokens * E * 2
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": f"qwen3-0.6b token embedding {V}x{E} bf16, {tokens} ids (int32)", "us_per_launch": round(us, 3),
+            "algorithmic_bytes_per_launch": nbytes, "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+            "kernel": "gather_rows_kernel", "timing": "256 back-to-back launches in one CUDA graph; table rows may hit L2"}
 
 
 def run_e2e(args, steps, k_pool, v_pool, err, world):
@@ -600,6 +626,7 @@ def main():
     ap.add_argument("--chunk", type=int, default=256, help="steps per captured CUDA graph")
     ap.add_argument("--pool-gb", type=float, default=150.0)
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--no-gather", action="store_true", help="skip the embedding-gather line")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

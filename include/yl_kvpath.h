@@ -69,6 +69,7 @@ typedef enum yl_status {
 #define YL_DEVERR_TABLE_ROW       0x80u /* index: table_index outside [0, num_table_rows)   */
 #define YL_DEVERR_TOKEN_COUNT     0x100u /* step: sum of new_len differs from num_tokens      */
 #define YL_DEVERR_TIMEOUT         0x200u /* store: a bulk copy did not complete within 2 s    */
+#define YL_DEVERR_INDEX_RANGE     0x400u /* gather: index outside [-1, num_rows)              */
 
 /*
  * Store (replaces yllang::StoreKVCache<kElementSize>,
@@ -198,6 +199,33 @@ typedef struct yl_step_args {
 } yl_step_args;
 
 YL_API int yl_kv_step(const yl_step_args *args, cudaStream_t stream);
+
+/*
+ * Row gather (replaces yllang::Index<kElementSize>, src/layers/index.cu:93-146,
+ * and its kernel IndexKernel, index.cu:49-77, used by VocabEmbeddingLayer,
+ * src/include/layers/vocab_embedding_layer.h:40-45): for i < num_indices,
+ *     row(out, i) <- row(table, indices[i])
+ * on the same copy engine as the store, with byte strides (the reference
+ * passes the table's row stride in elements where it adds bytes,
+ * index.cu:67,132).  An index outside [0, num_rows) zero-fills its output
+ * row; -1 does so silently, anything else also sets YL_DEVERR_INDEX_RANGE
+ * (when num_rows > 0; with num_rows <= 0 only negative indices are caught).
+ */
+typedef struct yl_gather_args {
+  const void *table;          /* source rows, [num_rows, row]                     */
+  void *out;                  /* destination rows, [num_indices, row]             */
+  const void *indices;        /* [num_indices] int32 or int64                     */
+  int32_t index_is_int64;
+  int32_t reserved;           /* must be 0                                        */
+  int64_t num_indices;
+  int64_t row_bytes;
+  int64_t table_row_stride;   /* bytes between table rows                         */
+  int64_t out_row_stride;     /* bytes between output rows                        */
+  int64_t num_rows;           /* table rows for range checks; <= 0: no check      */
+  uint32_t *error_word;
+} yl_gather_args;
+
+YL_API int yl_gather_rows(const yl_gather_args *args, cudaStream_t stream);
 
 /* Human-readable name of a yl_status value (static storage). */
 YL_API const char *yl_status_string(int status);

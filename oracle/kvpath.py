@@ -37,6 +37,7 @@ SLOTS_CAP = 0x10
 NEGATIVE_LEN = 0x20
 INDPTR_OVERFLOW = 0x40
 TABLE_ROW = 0x80
+INDEX_RANGE = 0x400
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -66,6 +67,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_build_index.argtypes = [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp,
                                          _vp, ctypes.c_int, _i64, _i64, _vp]
         L.oracle_max_threads.restype = ctypes.c_int
+        L.oracle_gather_rows.restype = _i64
+        L.oracle_gather_rows.argtypes = [_vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _vp]
         _lib = L
     return _lib
 
@@ -143,6 +146,20 @@ def build_index(prior_len, new_len, page_table: np.ndarray, page_size: int, tabl
     out["err"] = int(err.value)
     out["rc"] = int(rc)
     return out
+
+
+def gather(indices: np.ndarray, table: np.ndarray, num_rows: int | None = None) -> tuple[np.ndarray, int]:
+    """out[i] = table[indices[i]] (out-of-range rows zero); returns (out, error bits)."""
+    assert table.ndim == 2 and table.strides[1] == table.itemsize
+    idx = np.ascontiguousarray(indices)
+    assert idx.dtype in (np.int32, np.int64) and idx.ndim == 1
+    out = np.empty((idx.shape[0], table.shape[1]), table.dtype)
+    err = ctypes.c_uint32(0)
+    if idx.shape[0]:
+        lib().oracle_gather_rows(_ptr(table), _ptr(out), _ptr(idx), int(idx.dtype == np.int64), idx.shape[0],
+                                 table.shape[1] * table.itemsize, table.strides[0], out.strides[0],
+                                 table.shape[0] if num_rows is None else num_rows, ctypes.addressof(err))
+    return out, int(err.value)
 
 
 # ---------------------------------------------------------------------------

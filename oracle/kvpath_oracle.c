@@ -205,6 +205,34 @@ int oracle_build_index(const int32_t *prior_len, const int32_t *new_len, const i
   return rc;
 }
 
+/*
+ * Row gather: out[i] <- table[indices[i]], following IndexKernel
+ * (src/layers/index.cu:61-72: dst row i gets weights row indices[i]) with
+ * byte strides; an index outside [0, num_rows) (when num_rows > 0) or
+ * negative zero-fills its row, -1 silently, others also set bit 0x400.
+ * Returns the rows copied from the table.
+ */
+#define ORACLE_INDEX_RANGE 0x400u
+int64_t oracle_gather_rows(const uint8_t *table, uint8_t *out, const void *indices, int index_is_int64,
+                           int64_t num_indices, int64_t row_bytes, int64_t table_row_stride, int64_t out_row_stride,
+                           int64_t num_rows, uint32_t *error_word) {
+  int64_t copied = 0;
+  uint32_t err = 0;
+  for (int64_t i = 0; i < num_indices; ++i) {
+    const int64_t r = read_slot(indices, index_is_int64, i);
+    uint8_t *dst = out + i * out_row_stride;
+    if (r < 0 || (num_rows > 0 && r >= num_rows)) {
+      if (r != -1) err |= ORACLE_INDEX_RANGE;
+      memset(dst, 0, (size_t)row_bytes);
+      continue;
+    }
+    memcpy(dst, table + r * table_row_stride, (size_t)row_bytes);
+    ++copied;
+  }
+  if (error_word) *error_word |= err;
+  return copied;
+}
+
 /* Host threads available to this process (online processors). */
 int oracle_max_threads(void) {
   const long n = sysconf(_SC_NPROCESSORS_ONLN);

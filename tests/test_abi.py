@@ -48,7 +48,7 @@ def _c_layout(tmp_path, struct, fields):
 
 
 @pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs),
-                                        ("yl_step_args", _abi.StepArgs)])
+                                        ("yl_step_args", _abi.StepArgs), ("yl_gather_args", _abi.GatherArgs)])
 def test_struct_layout_matches_header(tmp_path, struct, cls):
     names = [f for f, _ in cls._fields_]
     c = _c_layout(tmp_path, struct, names)
@@ -118,6 +118,38 @@ def _index(**kw):
 def test_index_rejects_bad_arguments_on_host(kw, status):
     assert _abi.build_index_raw(_index(**kw), None) == status
     assert _abi.last_error().startswith("yl_build_index")
+
+
+def _gather(**kw):
+    a = _abi.GatherArgs()
+    base = dict(table=0x10000, out=0x20000, indices=0x3000, index_is_int64=0, num_indices=8, row_bytes=256,
+                table_row_stride=256, out_row_stride=256, num_rows=100)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(num_indices=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(row_bytes=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(reserved=1), _abi.YL_ERR_BAD_SIZE),
+    (dict(index_is_int64=2), _abi.YL_ERR_BAD_SIZE),
+    (dict(table=0), _abi.YL_ERR_NULL_ARG),
+    (dict(indices=0), _abi.YL_ERR_NULL_ARG),
+    (dict(out_row_stride=128), _abi.YL_ERR_BAD_SIZE),
+    (dict(indices=0x3002), _abi.YL_ERR_ALIGNMENT),
+    (dict(indices=0x3004, index_is_int64=1), _abi.YL_ERR_ALIGNMENT),
+    (dict(num_indices=1 << 31), _abi.YL_ERR_UNSUPPORTED),
+])
+def test_gather_rejects_bad_arguments_on_host(kw, status):
+    assert _abi.gather_rows_raw(_gather(**kw), None) == status
+    assert _abi.last_error().startswith("yl_gather_rows")
+
+
+def test_gather_zero_indices_is_noop_without_device():
+    assert _abi.gather_rows_raw(_gather(num_indices=0, table=0, out=0, indices=0), None) == _abi.YL_OK
+    assert yl.lib().yl_gather_rows(None, None) == _abi.YL_ERR_NULL_ARG
 
 
 def test_status_strings():

@@ -181,3 +181,23 @@ def test_store_slot_range_error():
     k = np.ones((2, 64), np.uint8)
     copied, err = orc.store(k, k, kc, vc, np.array([1, 7], np.int64), num_slots=4)
     assert copied == 2 and err == orc.SLOT_RANGE and kc[1].all() and not kc[[0, 2, 3]].any()
+
+
+def test_gather_oracle_matches_numpy_take():  # IndexKernel row copy (src/layers/index.cu:61-72)
+    rng = np.random.default_rng(5)
+    table = rng.integers(0, 1 << 16, size=(300, 96), dtype=np.uint16)
+    idx = rng.integers(0, 300, size=1000).astype(np.int32)
+    out, err = orc.gather(idx, table)
+    assert err == 0 and np.array_equal(out, table[idx])
+    out64, _ = orc.gather(idx.astype(np.int64), table)
+    assert np.array_equal(out64, out)
+
+
+def test_gather_oracle_out_of_range_rows_are_zero():
+    table = np.arange(40, dtype=np.uint8).reshape(10, 4) + 1
+    out, err = orc.gather(np.array([3, -1, 9], np.int64), table)
+    assert err == 0 and out[1].sum() == 0 and np.array_equal(out[[0, 2]], table[[3, 9]])
+    out, err = orc.gather(np.array([10, 2, -5], np.int64), table)
+    assert err == orc.INDEX_RANGE and out[0].sum() == 0 and out[2].sum() == 0 and np.array_equal(out[1], table[2])
+    out, err = orc.gather(np.zeros(0, np.int32), table)
+    assert out.shape == (0, 4) and err == 0

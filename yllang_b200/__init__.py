@@ -7,7 +7,10 @@ The hot path of one YLLang serving step, rebuilt for sm_100a:
   StoreKVCache / MHAKVCache::StoreKV);
 * ``build_index`` / ``yl_build_index``: the batch's kv_indptr, kv_indices,
   kv_last_page_len, qo_indptr and slot_mapping (the index work of YLLang's
-  BatchManager::NextBatch), in the paged-KV format flashinfer consumes.
+  BatchManager::NextBatch), in the paged-KV format flashinfer consumes;
+* ``kv_step`` / ``yl_kv_step``: both for one serving step;
+* ``gather_rows`` / ``yl_gather_rows``: the embedding-row gather (YLLang's
+  Index) on the same copy engine.
 
 The kernels live in libyl_kvpath.so (built in-tree); the C++ libtorch front
 end with YLLang's class names (MHAKVCache, KVCacheManager, BatchManager,
@@ -16,14 +19,16 @@ StoreKVCache) is the extension ``yllang_b200._C`` (``load_extension()``).
 from __future__ import annotations
 
 from ._abi import (DEVERR_INDICES_CAP, DEVERR_INDPTR_OVERFLOW, DEVERR_NEGATIVE_LEN, DEVERR_PAGE_RANGE,
-                   DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW, DEVERR_TOKEN_COUNT,
-                   KVPathError, lib)
-from .ops import BatchIndex, PanicError, build_index, kv_step, store_args, store_kv_cache
+                   DEVERR_INDEX_RANGE, DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW,
+                   DEVERR_TIMEOUT, DEVERR_TOKEN_COUNT, KVPathError, lib)
+from .ops import BatchIndex, PanicError, build_index, gather_rows, kv_step, store_args, store_kv_cache
 
 __all__ = [
-    "BatchIndex", "KVPathError", "PanicError", "build_index", "kv_step", "store_args", "store_kv_cache", "lib",
+    "BatchIndex", "KVPathError", "PanicError", "build_index", "gather_rows", "kv_step", "store_args",
+    "store_kv_cache", "lib",
     "load_extension", "DEVERR_SLOT_RANGE", "DEVERR_PAGE_RANGE", "DEVERR_ROW_OVERFLOW", "DEVERR_INDICES_CAP",
     "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW", "DEVERR_TOKEN_COUNT",
+    "DEVERR_TIMEOUT", "DEVERR_INDEX_RANGE",
 ]
 
 _ext = None

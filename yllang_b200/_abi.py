@@ -30,6 +30,7 @@ DEVERR_INDPTR_OVERFLOW = 0x40
 DEVERR_TABLE_ROW = 0x80
 DEVERR_TOKEN_COUNT = 0x100
 DEVERR_TIMEOUT = 0x200
+DEVERR_INDEX_RANGE = 0x400
 
 ABI_VERSION = 1
 
@@ -94,9 +95,27 @@ class StepArgs(ctypes.Structure):
     _fields_ = [("index", IndexArgs), ("store", StoreArgs)]
 
 
+class GatherArgs(ctypes.Structure):
+    """struct yl_gather_args."""
+
+    _fields_ = [
+        ("table", _vp),
+        ("out", _vp),
+        ("indices", _vp),
+        ("index_is_int64", _i32),
+        ("reserved", _i32),
+        ("num_indices", _i64),
+        ("row_bytes", _i64),
+        ("table_row_stride", _i64),
+        ("out_row_stride", _i64),
+        ("num_rows", _i64),
+        ("error_word", _vp),
+    ]
+
+
 # Every symbol include/yl_kvpath.h declares.
-EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_status_string", "yl_last_error",
-                    "yl_abi_version")
+EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_gather_rows", "yl_status_string",
+                    "yl_last_error", "yl_abi_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -124,6 +143,8 @@ def lib() -> ctypes.CDLL:
         L.yl_build_index.argtypes = [ctypes.POINTER(IndexArgs), _vp]
         L.yl_kv_step.restype = ctypes.c_int
         L.yl_kv_step.argtypes = [ctypes.POINTER(StepArgs), _vp]
+        L.yl_gather_rows.restype = ctypes.c_int
+        L.yl_gather_rows.argtypes = [ctypes.POINTER(GatherArgs), _vp]
         L.yl_status_string.restype = ctypes.c_char_p
         L.yl_status_string.argtypes = [ctypes.c_int]
         L.yl_last_error.restype = ctypes.c_char_p
@@ -159,3 +180,7 @@ def build_index_raw(args: IndexArgs, stream: int | None) -> int:
 
 def kv_step_raw(args: StepArgs, stream: int | None) -> int:
     return lib().yl_kv_step(ctypes.byref(args), stream)
+
+
+def gather_rows_raw(args: GatherArgs, stream: int | None) -> int:
+    return lib().yl_gather_rows(ctypes.byref(args), stream)

@@ -28,6 +28,14 @@ PYBIND11_MODULE(_C, m) {
   m.def("StoreKVCacheLayers", &StoreKVCacheLayers, py::arg("k"), py::arg("v"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("indices"), "every layer of a step in one launch: k, v [L, N, E]");
 
+  m.def(
+      "Index",
+      [](const torch::Tensor &indices, const torch::Tensor &weights, const torch::Tensor &destination) {
+        Index(indices, weights, destination);
+      },
+      py::arg("indices"), py::arg("weights"), py::arg("destination"),
+      "destination[i] = weights[indices[i]] (the embedding lookup of yllang::Index)");
+
   m.def("SetDistributedInfo", &SetDistributedInfo, py::arg("rank"), py::arg("size"));
   m.def("GetDistributedInfo", []() {
     const auto &d = GetDistributedInfo();

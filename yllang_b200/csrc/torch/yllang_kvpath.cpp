@@ -115,6 +115,32 @@ void StoreKVCacheLayers(const torch::Tensor &k, const torch::Tensor &v, const to
   LaunchStore(k, v, k_cache, v_cache, indices, k.size(0), k_cache.size(1), nullptr);
 }
 
+void Index(const torch::Tensor &indices, const torch::Tensor &weights, const torch::Tensor &destination) {
+  RuntimeCheck(weights.dim() == 2 && weights.stride(1) == 1, "Index: weights must be [V, E] with stride [*, 1]");
+  RuntimeCheck(destination.dim() == 2 && destination.stride(1) == 1 && destination.size(1) == weights.size(1),
+               "Index: destination must be [N, E] with stride [*, 1]");
+  CheckSameDeviceDtype(weights, {&destination}, "Index");
+  RuntimeCheck(indices.dim() == 1 && indices.size(0) == destination.size(0), "Index: indices must be [N]");
+  RuntimeCheck(indices.size(0) <= 1 || indices.stride(0) == 1, "Index: indices must have stride [1]");
+  RuntimeCheck(indices.scalar_type() == torch::kInt32 || indices.scalar_type() == torch::kInt64,
+               "Index: indices must be int32 or int64");
+  RuntimeCheck(indices.device() == weights.device(), "Index: indices on a different device");
+  if (indices.size(0) == 0) return;
+  const int64_t item = weights.element_size();
+  yl_gather_args a{};
+  a.table = weights.data_ptr();
+  a.out = destination.data_ptr();
+  a.indices = indices.data_ptr();
+  a.index_is_int64 = indices.scalar_type() == torch::kInt64 ? 1 : 0;
+  a.num_indices = indices.size(0);
+  a.row_bytes = weights.size(1) * item;
+  a.table_row_stride = weights.stride(0) * item;
+  a.out_row_stride = destination.stride(0) * item;
+  a.num_rows = weights.size(0);
+  const c10::cuda::CUDAGuard guard(weights.device());
+  CheckStatus(yl_gather_rows(&a, CurrentStream(weights)), "yl_gather_rows");
+}
+
 DistributedInfo &GetDistributedInfo() {
   static DistributedInfo instance(0, 1);
   return instance;

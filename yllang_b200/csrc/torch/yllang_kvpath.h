@@ -59,6 +59,21 @@ void StoreKVCacheLayers(const torch::Tensor &k, const torch::Tensor &v, const to
                         const torch::Tensor &v_cache, const torch::Tensor &indices);
 
 // ----------------------------------------------------------------------------
+// Row gather (the embedding lookup): destination[i] <- weights[indices[i]].
+// Contract of src/layers/index.cu:104-119: weights [V, E] with stride [ws, 1],
+// destination [N, E] with stride [ds, 1], indices [N] int32 or int64, one
+// device, one dtype.  Out-of-range indices give zero rows.
+// ----------------------------------------------------------------------------
+void Index(const torch::Tensor &indices, const torch::Tensor &weights, const torch::Tensor &destination);
+
+template <size_t kElementSize, size_t kThreadsPreBlock = 128, bool kUsePDL = false>
+void Index(const torch::Tensor &indices, const torch::Tensor &weights, const torch::Tensor &destination) {
+  RuntimeCheck(weights.dim() == 2 && static_cast<size_t>(weights.size(1) * weights.element_size()) == kElementSize,
+               "Index: kElementSize != row elements * dtype size");
+  Index(indices, weights, destination);
+}
+
+// ----------------------------------------------------------------------------
 // Tensor-parallel rank info (only the head split uses it)
 // ----------------------------------------------------------------------------
 class DistributedInfo {

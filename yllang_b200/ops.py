@@ -212,3 +212,35 @@ def kv_step(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torch.Te
     a.index = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, error_word)
     _abi.check(_abi.kv_step_raw(a, _stream(stream, k.device)))
     return out
+
+
+def gather_rows(indices: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None,
+                error_word: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out[i, :] = table[indices[i], :] (the embedding lookup); rows whose index
+    is outside the table come out zero (-1 silently, others also set
+    DEVERR_INDEX_RANGE).  Mirrors yllang::Index (src/layers/index.cu:93-146)
+    with the contract its TensorMatcher enforces (index.cu:104-119)."""
+    _check(table.dim() == 2 and table.stride(1) == 1, "table must be [V, E] with contiguous rows")
+    _check(table.is_cuda, "table must be a CUDA tensor")
+    _check(indices.dim() == 1 and (indices.stride(0) == 1 or indices.numel() <= 1), "indices must be [N], contiguous")
+    _check(indices.dtype in (torch.int32, torch.int64), "indices must be int32 or int64")
+    _check(indices.device == table.device, "indices on another device")
+    N, E = indices.shape[0], table.shape[1]
+    if out is None:
+        out = torch.empty(N, E, dtype=table.dtype, device=table.device)
+    _check(out.dim() == 2 and out.shape == (N, E) and out.stride(1) == 1, f"out must be [{N}, {E}] with contiguous rows")
+    _check(out.dtype == table.dtype and out.device == table.device, "out dtype/device must match the table")
+    if N == 0:
+        return out
+    item = table.element_size()
+    a = _abi.GatherArgs()
+    a.table, a.out, a.indices = table.data_ptr(), out.data_ptr(), indices.data_ptr()
+    a.index_is_int64 = int(indices.dtype == torch.int64)
+    a.num_indices = N
+    a.row_bytes = E * item
+    a.table_row_stride = table.stride(0) * item
+    a.out_row_stride = out.stride(0) * item
+    a.num_rows = table.shape[0]
+    a.error_word = error_word.data_ptr() if error_word is not None else None
+    _abi.check(_abi.gather_rows_raw(a, _stream(stream, table.device)))
+    return out
