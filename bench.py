@@ -539,6 +539,8 @@ def run_ours(args, world, rank, local):
         line["e2e"] = e2e
     if not args.no_gather:
         line["embedding_gather"] = bench_gather(dev, peak)
+    if not args.no_qkv:
+        line["qkv_norm_rope_store"] = bench_qkv(dev, peak)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_store_step_sample(b0, seconds=args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -566,6 +568,77 @@ def bench_gather(dev, peak: float, tokens: int = 4096, sets: int = 32) -> dict:
     return {"workload": f"qwen3-0.6b token embedding {V}x{E} bf16, {tokens} ids (int32)", "us_per_launch": round(us, 3),
             "algorithmic_bytes_per_launch": nbytes, "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
             "kernel": "gather_rows_kernel", "timing": "256 back-to-back launches in one CUDA graph; table rows may hit L2"}
+
+
+def bench_qkv(dev, peak: float) -> dict:
+    """One attention layer's input stage on the Qwen3-8B shape (32 Q heads,
+    8 KV heads, head_dim 128, bf16, rope_theta 1e6): the fused Q/K RMSNorm +
+    rotary + K/V store kernel against the unfused sequence of the same work
+    (flashinfer's Q norm, K norm and rotary kernels, then store_kv_cache), at
+    decode (256 tokens) and prefill (4096 tokens).  Inputs rotate over sets
+    larger than 2 x L2.  Algorithmic bytes per launch: Q/K/V rows read, Q and
+    K/V rows written, slots, positions and the tokens' cos/sin rows read."""
+    from yllang_b200.attention import _flashinfer
+
+    fi = _flashinfer()
+    Hq, Hk, D = 32, 8, 128
+    S = 1 << 16
+    k_cache = torch.zeros(S, Hk * D, dtype=torch.bfloat16, device=dev)
+    v_cache = torch.zeros_like(k_cache)
+    cs = yl.rope_cos_sin_cache(32768, D, theta=1e6, device=dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    qw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    out = {}
+    for name, N in (("decode", 256), ("prefill", 4096)):
+        set_bytes = N * (2 * Hq + 2 * Hk) * D * 2
+        R = max(2, math.ceil(2.2 * L2_BYTES / set_bytes))
+        sets = []
+        for r in range(R):
+            qkv = torch.randn(N, (Hq + 2 * Hk) * D, generator=g, device=dev).to(torch.bfloat16)
+            q = qkv[:, :Hq * D].view(N, Hq, D)
+            k = qkv[:, Hq * D:(Hq + Hk) * D].view(N, Hk, D)
+            v = qkv[:, (Hq + Hk) * D:].view(N, Hk, D)
+            slots = torch.randperm(S, generator=g, device=dev)[:N]
+            pos = torch.randint(0, 32768, (N,), generator=g, device=dev)
+            sets.append((qkv, q, k, v, slots, pos, torch.empty(N, Hq, D, dtype=torch.bfloat16, device=dev)))
+
+        def fused(r):
+            _, q, k, v, slots, pos, q_out = sets[r]
+            return [lambda: yl.qkv_norm_rope_store(q, k, v, k_cache, v_cache, slots, q_weight=qw, k_weight=kw,
+                                                   eps=1e-6, cos_sin_cache=cs, positions=pos, q_out=q_out)]
+
+        def unfused(r):
+            _, q, k, v, slots, pos, q_out = sets[r]
+            kn = torch.empty(N, Hk, D, dtype=torch.bfloat16, device=dev)
+
+            def rope():
+                fi.rope.apply_rope_with_cos_sin_cache_inplace(pos, q_out.view(N, Hq * D), kn.view(N, Hk * D), D, cs,
+                                                              is_neox=True)
+            return [lambda: fi.norm.rmsnorm(q, qw, eps=1e-6, out=q_out),
+                    lambda: fi.norm.rmsnorm(k, kw, eps=1e-6, out=kn), rope,
+                    lambda: yl.store_kv_cache(kn.view(N, Hk * D), v.reshape(N, Hk * D), k_cache, v_cache, slots)]
+
+        for fn in fused(0) + unfused(0):
+            fn()
+        torch.cuda.synchronize()
+        us = per_launch_us(R, fused, 128)
+        try:
+            us_unfused = per_launch_us(R, unfused, 128)
+            how = "4 launches in one CUDA graph"
+        except Exception as e:  # a library op that cannot be captured: time it eagerly
+            us_unfused = None
+            how = f"not captured: {type(e).__name__}"
+        nbytes = N * (2 * Hq + 4 * Hk) * D * 2 + N * 16 + N * D * 4
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"tokens": N, "us_per_launch": round(us, 3), "algorithmic_bytes_per_launch": nbytes,
+                     "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+                     "unfused_us": None if us_unfused is None else round(us_unfused, 3), "unfused_timing": how}
+        del sets
+    out["workload"] = "qwen3-8b attention input, 32 q heads, 8 kv heads, head_dim 128, bf16, one layer"
+    out["kernel"] = "qkv_norm_rope_store_kernel"
+    out["unfused"] = "flashinfer rmsnorm(q), rmsnorm(k), apply_rope_with_cos_sin_cache_inplace, store_kv_cache"
+    return out
 
 
 def run_e2e(args, steps, k_pool, v_pool, err, world):
@@ -627,6 +700,7 @@ def main():
     ap.add_argument("--pool-gb", type=float, default=150.0)
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-gather", action="store_true", help="skip the embedding-gather line")
+    ap.add_argument("--no-qkv", action="store_true", help="skip the fused norm/rotary/store line")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -70,6 +70,7 @@ typedef enum yl_status {
 #define YL_DEVERR_TOKEN_COUNT     0x100u /* step: sum of new_len differs from num_tokens      */
 #define YL_DEVERR_TIMEOUT         0x200u /* store: a bulk copy did not complete within 2 s    */
 #define YL_DEVERR_INDEX_RANGE     0x400u /* gather: index outside [-1, num_rows)              */
+#define YL_DEVERR_POSITION_RANGE  0x800u /* qkv store: position outside [0, max_position)     */
 
 /*
  * Store (replaces yllang::StoreKVCache<kElementSize>,
@@ -226,6 +227,66 @@ typedef struct yl_gather_args {
 } yl_gather_args;
 
 YL_API int yl_gather_rows(const yl_gather_args *args, cudaStream_t stream);
+
+/*
+ * One layer's attention input, fused: per-head RMSNorm of Q and K, rotary
+ * embedding of Q and K, then Q written out and K/V stored into the pool by
+ * slot, reading every input row once.  Replaces the sequence the reference's
+ * attention layer is built for (src/include/layers/attention.h:22-68): Q/K
+ * RMSNorm through flashinfer::norm::QKRMSNorm (src/layers/rsm_norm.cu:35-52,
+ * out = x * rsqrt(mean(x^2) + eps) * w over head_dim, fp32 arithmetic),
+ * rotary embedding at the model config's rope_theta
+ * (src/models/model_config.cpp:38) and StoreKVCache of K and V.  For token i
+ * and head h (rows of head_dim elements):
+ *     x  = q[i, h]            (or k[i, h])
+ *     x  = T(x * rsqrt(sum(x^2) / head_dim + eps) * w)      if w != NULL
+ *     x  = rotate(x, cos_sin_cache[positions[i]])           if cache != NULL
+ *     q_out[i, h] = T(x);  k_cache[slots[i], h] = T(x);  v_cache[slots[i], h] = v[i, h]
+ * The norm output is rounded to T before the rotation, as the unfused
+ * norm-then-rope sequence stores it.  rotate: neox halves (element j pairs
+ * with j + head_dim/2) or, with rope_interleaved, GPT-J pairs (2j, 2j+1);
+ * cos_sin_cache[p] holds head_dim/2 cosines then head_dim/2 sines (fp32), the
+ * layout of flashinfer's apply_rope_with_cos_sin_cache.  Slot -1 skips the
+ * token's K/V rows silently, other out-of-range slots set
+ * YL_DEVERR_SLOT_RANGE; a position outside [0, max_position) sets
+ * YL_DEVERR_POSITION_RANGE and leaves that token's Q, K and V rows unwritten.
+ * head_dim is 64, 128 or 256; T is bf16 or fp16.  No counterpart kernel in
+ * the reference (its attention forward is a placeholder, attention.h:55).
+ */
+#define YL_DTYPE_BF16 0
+#define YL_DTYPE_F16  1
+typedef struct yl_qkv_store_args {
+  const void *q;              /* [N, num_q_heads, head_dim] rows, q_row_stride apart   */
+  const void *k;              /* [N, num_kv_heads, head_dim]                           */
+  const void *v;              /* [N, num_kv_heads, head_dim]                           */
+  void *q_out;                /* [N, num_q_heads, head_dim]; may equal q               */
+  void *k_cache;              /* pool rows [num_slots, num_kv_heads * head_dim]        */
+  void *v_cache;
+  const void *slots;          /* [N] int32 or int64                                    */
+  const void *q_weight;       /* [head_dim] RMSNorm weight of Q (type T); NULL: none   */
+  const void *k_weight;       /* [head_dim] RMSNorm weight of K; NULL: none            */
+  const float *cos_sin_cache; /* [max_position, head_dim] fp32; NULL: no rotation      */
+  const void *positions;      /* [N] int32 or int64 (needed with cos_sin_cache)        */
+  int32_t dtype;              /* YL_DTYPE_BF16 or YL_DTYPE_F16                         */
+  int32_t slot_is_int64;
+  int32_t position_is_int64;
+  int32_t rope_interleaved;   /* 0: neox halves, 1: GPT-J pairs                        */
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float eps;
+  int64_t num_tokens;
+  int64_t q_row_stride;       /* bytes between tokens of q                             */
+  int64_t k_row_stride;
+  int64_t v_row_stride;
+  int64_t q_out_row_stride;
+  int64_t cache_row_stride;   /* bytes between pool rows                               */
+  int64_t num_slots;          /* pool rows for range checks; <= 0: no check            */
+  int64_t max_position;       /* rows of cos_sin_cache                                 */
+  uint32_t *error_word;
+} yl_qkv_store_args;
+
+YL_API int yl_qkv_norm_rope_store(const yl_qkv_store_args *args, cudaStream_t stream);
 
 /* Human-readable name of a yl_status value (static storage). */
 YL_API const char *yl_status_string(int status);

@@ -38,6 +38,7 @@ NEGATIVE_LEN = 0x20
 INDPTR_OVERFLOW = 0x40
 TABLE_ROW = 0x80
 INDEX_RANGE = 0x400
+POSITION_RANGE = 0x800
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -160,6 +161,79 @@ def gather(indices: np.ndarray, table: np.ndarray, num_rows: int | None = None) 
                                  table.shape[1] * table.itemsize, table.strides[0], out.strides[0],
                                  table.shape[0] if num_rows is None else num_rows, ctypes.addressof(err))
     return out, int(err.value)
+
+
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values rounded to bf16 or fp16 (round to nearest even), as float32."""
+    x = np.asarray(x, np.float32)
+    if dtype == "fp16":
+        with np.errstate(over="ignore"):  # beyond fp16's range: inf, as the device conversion gives
+            return x.astype(np.float16).astype(np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    r = (b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000
+    out = r.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), x, out)
+
+
+def qkv_norm_rope_store(q, k, v, k_cache, v_cache, slots, q_weight=None, k_weight=None, eps=1e-6, cos_sin=None,
+                        positions=None, interleaved=False, dtype="bf16", num_slots=None):
+    """Restatement of the unfused sequence the fused kernel replaces:
+    per-head RMSNorm (flashinfer::norm::QKRMSNorm as called at
+    src/layers/rsm_norm.cu:49: fp32 sum of squares, x * rsqrt(ss / d + eps) * w,
+    one rounding to the storage type), then the rotary embedding of
+    apply_rope_with_cos_sin_cache (fp32, one rounding), then the store of
+    store_kv_cache.cu:60-72.  Arrays are float32 holding values of the
+    storage type: q [N, Hq, D], k/v [N, Hk, D], caches [S, Hk, D] (updated in
+    place).  Returns (q_out, error bits); rows with a bad position stay
+    unwritten (NaN in q_out)."""
+    q, k, v = (np.asarray(a, np.float32) for a in (q, k, v))
+    N, Hq, D = q.shape
+    S = k_cache.shape[0] if num_slots is None else num_slots
+    err = 0
+
+    def norm(x, w):
+        if w is None:
+            return x
+        ss = np.sum(x * x, axis=-1, dtype=np.float32, keepdims=True)
+        r = (np.float32(1.0) / np.sqrt(ss / np.float32(D) + np.float32(eps))).astype(np.float32)
+        return round_to(x * r * np.asarray(w, np.float32), dtype)
+
+    def rope(x, cs):
+        c, s = cs[:, None, : D // 2], cs[:, None, D // 2:]
+        y = np.empty_like(x)
+        if interleaved:
+            a, b = x[..., 0::2], x[..., 1::2]
+            y[..., 0::2] = a * c - b * s
+            y[..., 1::2] = b * c + a * s
+        else:
+            a, b = x[..., : D // 2], x[..., D // 2:]
+            y[..., : D // 2] = a * c - b * s
+            y[..., D // 2:] = b * c + a * s
+        return y
+
+    qn, kn = norm(q, q_weight), norm(k, k_weight)
+    ok = np.ones(N, bool)
+    if cos_sin is not None:
+        pos = np.asarray(positions, np.int64)
+        ok = (pos >= 0) & (pos < cos_sin.shape[0])
+        if not ok.all():
+            err |= POSITION_RANGE
+        cs = np.asarray(cos_sin, np.float32)[np.where(ok, pos, 0)]
+        qn, kn = rope(qn, cs), rope(kn, cs)
+    q_out = np.full_like(q, np.nan)
+    q_out[ok] = round_to(qn[ok], dtype)
+    kn = round_to(kn, dtype)
+    for i in range(N):
+        if not ok[i]:
+            continue
+        s_ = int(slots[i])
+        if s_ < 0 or s_ >= S:
+            if s_ != -1:
+                err |= SLOT_RANGE
+            continue
+        k_cache[s_] = kn[i]
+        v_cache[s_] = v[i]
+    return q_out, err
 
 
 # ---------------------------------------------------------------------------

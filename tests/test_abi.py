@@ -48,7 +48,8 @@ def _c_layout(tmp_path, struct, fields):
 
 
 @pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs),
-                                        ("yl_step_args", _abi.StepArgs), ("yl_gather_args", _abi.GatherArgs)])
+                                        ("yl_step_args", _abi.StepArgs), ("yl_gather_args", _abi.GatherArgs),
+                                        ("yl_qkv_store_args", _abi.QkvStoreArgs)])
 def test_struct_layout_matches_header(tmp_path, struct, cls):
     names = [f for f, _ in cls._fields_]
     c = _c_layout(tmp_path, struct, names)
@@ -150,6 +151,48 @@ def test_gather_rejects_bad_arguments_on_host(kw, status):
 def test_gather_zero_indices_is_noop_without_device():
     assert _abi.gather_rows_raw(_gather(num_indices=0, table=0, out=0, indices=0), None) == _abi.YL_OK
     assert yl.lib().yl_gather_rows(None, None) == _abi.YL_ERR_NULL_ARG
+
+
+def _qkv(**kw):
+    a = _abi.QkvStoreArgs()
+    base = dict(q=0x10000, k=0x20000, v=0x30000, q_out=0x40000, k_cache=0x100000, v_cache=0x200000, slots=0x5000,
+                dtype=0, slot_is_int64=1, num_q_heads=32, num_kv_heads=8, head_dim=128, eps=1e-6, num_tokens=4,
+                q_row_stride=8192, k_row_stride=2048, v_row_stride=2048, q_out_row_stride=8192,
+                cache_row_stride=2048, num_slots=1000)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(num_tokens=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(dtype=2), _abi.YL_ERR_BAD_SIZE),
+    (dict(head_dim=96), _abi.YL_ERR_UNSUPPORTED),
+    (dict(num_kv_heads=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(rope_interleaved=2), _abi.YL_ERR_BAD_SIZE),
+    (dict(eps=-1.0), _abi.YL_ERR_BAD_SIZE),
+    (dict(eps=float("nan")), _abi.YL_ERR_BAD_SIZE),
+    (dict(k=0), _abi.YL_ERR_NULL_ARG),
+    (dict(q_out=0), _abi.YL_ERR_NULL_ARG),
+    (dict(cos_sin_cache=0x9000), _abi.YL_ERR_BAD_SIZE),
+    (dict(cos_sin_cache=0x9000, positions=0x6000, max_position=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(cache_row_stride=1024), _abi.YL_ERR_BAD_SIZE),
+    (dict(q_row_stride=4096), _abi.YL_ERR_BAD_SIZE),
+    (dict(k=0x20004), _abi.YL_ERR_ALIGNMENT),
+    (dict(k_weight=0x7002), _abi.YL_ERR_ALIGNMENT),
+    (dict(cos_sin_cache=0x9008, positions=0x6000, max_position=10), _abi.YL_ERR_ALIGNMENT),
+    (dict(slots=0x5004), _abi.YL_ERR_ALIGNMENT),
+    (dict(num_tokens=1 << 26), _abi.YL_ERR_UNSUPPORTED),
+])
+def test_qkv_store_rejects_bad_arguments_on_host(kw, status):
+    assert _abi.qkv_store_raw(_qkv(**kw), None) == status
+    assert _abi.last_error().startswith("yl_qkv_norm_rope_store")
+
+
+def test_qkv_store_zero_tokens_is_noop_without_device():
+    assert _abi.qkv_store_raw(_qkv(num_tokens=0, q=0, k=0, v=0, slots=0), None) == _abi.YL_OK
+    assert yl.lib().yl_qkv_norm_rope_store(None, None) == _abi.YL_ERR_NULL_ARG
 
 
 def test_status_strings():

@@ -201,3 +201,68 @@ def test_gather_oracle_out_of_range_rows_are_zero():
     assert err == orc.INDEX_RANGE and out[0].sum() == 0 and out[2].sum() == 0 and np.array_equal(out[1], table[2])
     out, err = orc.gather(np.zeros(0, np.int32), table)
     assert out.shape == (0, 4) and err == 0
+
+
+def test_round_to_matches_torch_conversions():
+    import torch
+
+    rng = np.random.default_rng(6)
+    x = (rng.standard_normal(100000) * np.exp(rng.uniform(-20, 20, 100000))).astype(np.float32)
+    x[:4] = [0.0, -0.0, 1.0 + 2.0 ** -8, 1.0 + 3 * 2.0 ** -8]  # ties round to even
+    for dtype, tdt in (("bf16", torch.bfloat16), ("fp16", torch.float16)):
+        want = torch.from_numpy(x).to(tdt).float().numpy()
+        got = orc.round_to(x, dtype)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), dtype
+
+
+def _qkv_case(N=6, Hq=4, Hk=2, D=64, seed=0, S=32):
+    rng = np.random.default_rng(seed)
+    r = lambda *s: orc.round_to(rng.standard_normal(s).astype(np.float32), "bf16")
+    q, k, v = r(N, Hq, D), r(N, Hk, D), r(N, Hk, D)
+    qw, kw = orc.round_to(1 + 0.1 * rng.standard_normal(D).astype(np.float32), "bf16"), r(D)
+    pos = rng.integers(0, 100, N)
+    ang = pos[:, None] * (1e4 ** (-np.arange(0, D, 2) / D))[None, :]
+    cache = np.concatenate([np.cos(np.arange(128)[:, None] * (1e4 ** (-np.arange(0, D, 2) / D))),
+                            np.sin(np.arange(128)[:, None] * (1e4 ** (-np.arange(0, D, 2) / D)))], 1).astype(np.float32)
+    slots = rng.permutation(S)[:N]
+    return q, k, v, qw, kw, pos, cache, slots, ang
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_qkv_oracle_against_float64_formula(interleaved):
+    """The restatement against the textbook formulas in float64 (norm, then
+    rotation of pairs by the position's angles)."""
+    q, k, v, qw, kw, pos, cache, slots, ang = _qkv_case()
+    D = q.shape[-1]
+    kc = np.zeros((32, 2, D), np.float32)
+    vc = np.zeros_like(kc)
+    q_out, err = orc.qkv_norm_rope_store(q, k, v, kc, vc, slots, qw, kw, 1e-6, cache, pos, interleaved)
+    assert err == 0
+
+    def ref(x, w):
+        x = x.astype(np.float64)
+        x = x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6) * w
+        c, s = np.cos(ang)[:, None], np.sin(ang)[:, None]
+        a, b = (x[..., 0::2], x[..., 1::2]) if interleaved else (x[..., :D // 2], x[..., D // 2:])
+        y = np.empty_like(x)
+        if interleaved:
+            y[..., 0::2], y[..., 1::2] = a * c - b * s, b * c + a * s
+        else:
+            y[..., :D // 2], y[..., D // 2:] = a * c - b * s, b * c + a * s
+        return y
+
+    np.testing.assert_allclose(q_out, ref(q, qw), atol=3e-2, rtol=3e-2)
+    np.testing.assert_allclose(kc[slots], ref(k, kw), atol=3e-2, rtol=3e-2)
+    assert np.array_equal(vc[slots], v)
+
+
+def test_qkv_oracle_error_bits():
+    q, k, v, qw, kw, pos, cache, slots, _ = _qkv_case()
+    kc = np.zeros((32, 2, 64), np.float32)
+    vc = np.zeros_like(kc)
+    pos[1], slots[2], slots[3] = 500, -1, 40
+    q_out, err = orc.qkv_norm_rope_store(q, k, v, kc, vc, slots, qw, kw, 1e-6, cache, pos)
+    assert err == orc.POSITION_RANGE | orc.SLOT_RANGE
+    assert np.isnan(q_out[1]).all() and not np.isnan(q_out[[0, 2, 3, 4, 5]]).any()
+    written = {int(s) for i, s in enumerate(slots) if i not in (1, 2, 3)}
+    assert {int(s) for s in np.nonzero(vc.any(axis=(1, 2)))[0]} == written

@@ -10,7 +10,9 @@ The hot path of one YLLang serving step, rebuilt for sm_100a:
   BatchManager::NextBatch), in the paged-KV format flashinfer consumes;
 * ``kv_step`` / ``yl_kv_step``: both for one serving step;
 * ``gather_rows`` / ``yl_gather_rows``: the embedding-row gather (YLLang's
-  Index) on the same copy engine.
+  Index) on the same copy engine;
+* ``qkv_norm_rope_store`` / ``yl_qkv_norm_rope_store``: one layer's Q/K
+  RMSNorm and rotary embedding fused with the K/V store.
 
 The kernels live in libyl_kvpath.so (built in-tree); the C++ libtorch front
 end with YLLang's class names (MHAKVCache, KVCacheManager, BatchManager,
@@ -20,15 +22,16 @@ from __future__ import annotations
 
 from ._abi import (DEVERR_INDICES_CAP, DEVERR_INDPTR_OVERFLOW, DEVERR_NEGATIVE_LEN, DEVERR_PAGE_RANGE,
                    DEVERR_INDEX_RANGE, DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW,
-                   DEVERR_TIMEOUT, DEVERR_TOKEN_COUNT, KVPathError, lib)
-from .ops import BatchIndex, PanicError, build_index, gather_rows, kv_step, store_args, store_kv_cache
+                   DEVERR_POSITION_RANGE, DEVERR_TIMEOUT, DEVERR_TOKEN_COUNT, KVPathError, lib)
+from .ops import (BatchIndex, PanicError, build_index, gather_rows, kv_step, qkv_norm_rope_store, rope_cos_sin_cache,
+                  store_args, store_kv_cache)
 
 __all__ = [
-    "BatchIndex", "KVPathError", "PanicError", "build_index", "gather_rows", "kv_step", "store_args",
-    "store_kv_cache", "lib",
+    "BatchIndex", "KVPathError", "PanicError", "build_index", "gather_rows", "kv_step", "qkv_norm_rope_store",
+    "rope_cos_sin_cache", "store_args", "store_kv_cache", "lib",
     "load_extension", "DEVERR_SLOT_RANGE", "DEVERR_PAGE_RANGE", "DEVERR_ROW_OVERFLOW", "DEVERR_INDICES_CAP",
     "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW", "DEVERR_TOKEN_COUNT",
-    "DEVERR_TIMEOUT", "DEVERR_INDEX_RANGE",
+    "DEVERR_TIMEOUT", "DEVERR_INDEX_RANGE", "DEVERR_POSITION_RANGE",
 ]
 
 _ext = None

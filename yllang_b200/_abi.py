@@ -31,6 +31,7 @@ DEVERR_TABLE_ROW = 0x80
 DEVERR_TOKEN_COUNT = 0x100
 DEVERR_TIMEOUT = 0x200
 DEVERR_INDEX_RANGE = 0x400
+DEVERR_POSITION_RANGE = 0x800
 
 ABI_VERSION = 1
 
@@ -113,9 +114,46 @@ class GatherArgs(ctypes.Structure):
     ]
 
 
+class QkvStoreArgs(ctypes.Structure):
+    """struct yl_qkv_store_args."""
+
+    _fields_ = [
+        ("q", _vp),
+        ("k", _vp),
+        ("v", _vp),
+        ("q_out", _vp),
+        ("k_cache", _vp),
+        ("v_cache", _vp),
+        ("slots", _vp),
+        ("q_weight", _vp),
+        ("k_weight", _vp),
+        ("cos_sin_cache", _vp),
+        ("positions", _vp),
+        ("dtype", _i32),
+        ("slot_is_int64", _i32),
+        ("position_is_int64", _i32),
+        ("rope_interleaved", _i32),
+        ("num_q_heads", _i32),
+        ("num_kv_heads", _i32),
+        ("head_dim", _i32),
+        ("eps", ctypes.c_float),
+        ("num_tokens", _i64),
+        ("q_row_stride", _i64),
+        ("k_row_stride", _i64),
+        ("v_row_stride", _i64),
+        ("q_out_row_stride", _i64),
+        ("cache_row_stride", _i64),
+        ("num_slots", _i64),
+        ("max_position", _i64),
+        ("error_word", _vp),
+    ]
+
+
+YL_DTYPE_BF16, YL_DTYPE_F16 = 0, 1
+
 # Every symbol include/yl_kvpath.h declares.
-EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_gather_rows", "yl_status_string",
-                    "yl_last_error", "yl_abi_version")
+EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_gather_rows", "yl_qkv_norm_rope_store",
+                    "yl_status_string", "yl_last_error", "yl_abi_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -145,6 +183,8 @@ def lib() -> ctypes.CDLL:
         L.yl_kv_step.argtypes = [ctypes.POINTER(StepArgs), _vp]
         L.yl_gather_rows.restype = ctypes.c_int
         L.yl_gather_rows.argtypes = [ctypes.POINTER(GatherArgs), _vp]
+        L.yl_qkv_norm_rope_store.restype = ctypes.c_int
+        L.yl_qkv_norm_rope_store.argtypes = [ctypes.POINTER(QkvStoreArgs), _vp]
         L.yl_status_string.restype = ctypes.c_char_p
         L.yl_status_string.argtypes = [ctypes.c_int]
         L.yl_last_error.restype = ctypes.c_char_p
@@ -184,3 +224,7 @@ def kv_step_raw(args: StepArgs, stream: int | None) -> int:
 
 def gather_rows_raw(args: GatherArgs, stream: int | None) -> int:
     return lib().yl_gather_rows(ctypes.byref(args), stream)
+
+
+def qkv_store_raw(args: QkvStoreArgs, stream: int | None) -> int:
+    return lib().yl_qkv_norm_rope_store(ctypes.byref(args), stream)

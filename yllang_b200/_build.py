@@ -23,7 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libyl_kvpath.so")
 
-CUDA_SOURCES = ["common.cu", "kv_store.cu", "index_build.cu", "kv_step.cu", "gather.cu"]
+CUDA_SOURCES = ["common.cu", "kv_store.cu", "index_build.cu", "kv_step.cu", "gather.cu", "qkv_store.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -29,20 +29,29 @@ _FI_BASE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "f
 
 def _flashinfer():
     os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", _FI_BASE)
+    # the CUDA build of flashinfer's norm kernels: the one the reference's
+    # RSMNormWithoutResidual calls (src/layers/rsm_norm.cu:29,49)
+    os.environ.setdefault("FLASHINFER_USE_CUDA_NORM", "1")
     import flashinfer
 
     return flashinfer
 
 
 def prebuild(head_dims=(64, 128, 256), dtype=torch.bfloat16) -> None:
-    """Compile flashinfer's paged-decode kernels for sm_100a into the package's
-    build folder (no GPU needed)."""
+    """Compile flashinfer's paged-decode kernels, and the norm and rotary
+    kernels the fused Q/K norm + store is checked against, for sm_100a into
+    the package's build folder (no GPU needed)."""
     os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", _FI_BASE)
     os.environ.setdefault("FLASHINFER_CUDA_ARCH_LIST", "10.0")
+    os.environ.setdefault("FLASHINFER_USE_CUDA_NORM", "1")
     from flashinfer.decode import get_batch_decode_module
+    from flashinfer.norm import get_norm_module
+    from flashinfer.rope import get_rope_module
 
     for d in head_dims:
         get_batch_decode_module(dtype, dtype, dtype, torch.int32, d, d, 0, False, False)
+    get_norm_module()
+    get_rope_module()
 
 
 class PagedDecodeAttention:

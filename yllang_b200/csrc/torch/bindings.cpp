@@ -36,6 +36,17 @@ PYBIND11_MODULE(_C, m) {
       py::arg("indices"), py::arg("weights"), py::arg("destination"),
       "destination[i] = weights[indices[i]] (the embedding lookup of yllang::Index)");
 
+  py::class_<QKNormRope>(m, "QKNormRope")
+      .def(py::init<>())
+      .def_readwrite("q_weight", &QKNormRope::q_weight)
+      .def_readwrite("k_weight", &QKNormRope::k_weight)
+      .def_readwrite("eps", &QKNormRope::eps)
+      .def_readwrite("cos_sin_cache", &QKNormRope::cos_sin_cache)
+      .def_readwrite("positions", &QKNormRope::positions)
+      .def_readwrite("interleaved", &QKNormRope::interleaved);
+  m.def("QKNormRopeStoreKV", &QKNormRopeStoreKV, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("indices"), py::arg("opts"), py::arg("q_out"));
+
   m.def("SetDistributedInfo", &SetDistributedInfo, py::arg("rank"), py::arg("size"));
   m.def("GetDistributedInfo", []() {
     const auto &d = GetDistributedInfo();
@@ -59,6 +70,8 @@ PYBIND11_MODULE(_C, m) {
            py::arg("zero_fill") = true)
       .def("StoreKV", &MHAKVCache::StoreKV, py::arg("k"), py::arg("v"), py::arg("loc"), py::arg("layer_id"))
       .def("StoreKVAllLayers", &MHAKVCache::StoreKVAllLayers, py::arg("k"), py::arg("v"), py::arg("loc"))
+      .def("StoreKVNormRope", &MHAKVCache::StoreKVNormRope, py::arg("q"), py::arg("k"), py::arg("v"),
+           py::arg("loc"), py::arg("layer_id"), py::arg("opts"), py::arg("q_out") = py::none())
       .def("KCache", &MHAKVCache::KCache)
       .def("VCache", &MHAKVCache::VCache)
       .def("NumLayers", &MHAKVCache::NumLayers)

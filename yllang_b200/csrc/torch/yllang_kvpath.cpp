@@ -141,6 +141,80 @@ void Index(const torch::Tensor &indices, const torch::Tensor &weights, const tor
   CheckStatus(yl_gather_rows(&a, CurrentStream(weights)), "yl_gather_rows");
 }
 
+void QKNormRopeStoreKV(const torch::Tensor &q, const torch::Tensor &k, const torch::Tensor &v,
+                       const torch::Tensor &k_cache, const torch::Tensor &v_cache, const torch::Tensor &indices,
+                       const QKNormRope &opts, const torch::Tensor &q_out) {
+  const auto heads_ok = [](const torch::Tensor &t) { return t.dim() == 3 && t.stride(2) == 1 && t.stride(1) == t.size(2); };
+  RuntimeCheck(heads_ok(q) && heads_ok(k) && heads_ok(v) && heads_ok(q_out),
+               "QKNormRopeStoreKV: q, k, v, q_out must be [N, heads, D] with contiguous heads");
+  const int64_t n = q.size(0), hq = q.size(1), d = q.size(2), hk = k.size(1);
+  RuntimeCheck(k.sizes() == v.sizes() && k.size(0) == n && k.size(2) == d && q_out.sizes() == q.sizes(),
+               "QKNormRopeStoreKV: shapes of q, k, v, q_out disagree");
+  RuntimeCheck(q.scalar_type() == torch::kBFloat16 || q.scalar_type() == torch::kHalf,
+               "QKNormRopeStoreKV: dtype must be bf16 or fp16");
+  CheckSameDeviceDtype(q, {&k, &v, &q_out, &k_cache, &v_cache}, "QKNormRopeStoreKV");
+  for (const auto *c : {&k_cache, &v_cache})
+    RuntimeCheck(c->dim() == 2 && c->size(1) == hk * d && c->stride(1) == 1,
+                 "QKNormRopeStoreKV: caches must be [S, Hk * D] with unit column stride");
+  RuntimeCheck(k_cache.sizes() == v_cache.sizes() && k_cache.stride(0) == v_cache.stride(0),
+               "QKNormRopeStoreKV: k_cache and v_cache must share shape and row stride");
+  RuntimeCheck(indices.dim() == 1 && indices.size(0) == n && (n <= 1 || indices.stride(0) == 1) &&
+                   (indices.scalar_type() == torch::kInt32 || indices.scalar_type() == torch::kInt64) &&
+                   indices.device() == q.device(),
+               "QKNormRopeStoreKV: indices must be contiguous int32/int64 [N] on q's device");
+  for (const auto *w : {&opts.q_weight, &opts.k_weight})
+    if (*w)
+      RuntimeCheck((*w)->dim() == 1 && (*w)->size(0) == d && (*w)->is_contiguous() &&
+                       (*w)->scalar_type() == q.scalar_type() && (*w)->device() == q.device(),
+                   "QKNormRopeStoreKV: norm weights must be contiguous [D] of q's dtype and device");
+  if (opts.cos_sin_cache) {
+    const auto &cs = *opts.cos_sin_cache;
+    RuntimeCheck(cs.dim() == 2 && cs.size(1) == d && cs.is_contiguous() && cs.scalar_type() == torch::kFloat32 &&
+                     cs.device() == q.device(),
+                 "QKNormRopeStoreKV: cos_sin_cache must be contiguous fp32 [max_position, D]");
+    RuntimeCheck(opts.positions && opts.positions->dim() == 1 && opts.positions->size(0) == n &&
+                     (n <= 1 || opts.positions->stride(0) == 1) &&
+                     (opts.positions->scalar_type() == torch::kInt32 ||
+                      opts.positions->scalar_type() == torch::kInt64) &&
+                     opts.positions->device() == q.device(),
+                 "QKNormRopeStoreKV: positions must be contiguous int32/int64 [N] on q's device");
+  }
+  if (n == 0) return;
+  const int64_t item = q.element_size();
+  yl_qkv_store_args a{};
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.q_out = q_out.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.slots = indices.data_ptr();
+  a.q_weight = opts.q_weight ? opts.q_weight->data_ptr() : nullptr;
+  a.k_weight = opts.k_weight ? opts.k_weight->data_ptr() : nullptr;
+  if (opts.cos_sin_cache) {
+    a.cos_sin_cache = opts.cos_sin_cache->data_ptr<float>();
+    a.positions = opts.positions->data_ptr();
+    a.position_is_int64 = opts.positions->scalar_type() == torch::kInt64 ? 1 : 0;
+    a.max_position = opts.cos_sin_cache->size(0);
+  }
+  a.dtype = q.scalar_type() == torch::kBFloat16 ? YL_DTYPE_BF16 : YL_DTYPE_F16;
+  a.slot_is_int64 = indices.scalar_type() == torch::kInt64 ? 1 : 0;
+  a.rope_interleaved = opts.interleaved ? 1 : 0;
+  a.num_q_heads = static_cast<int32_t>(hq);
+  a.num_kv_heads = static_cast<int32_t>(hk);
+  a.head_dim = static_cast<int32_t>(d);
+  a.eps = static_cast<float>(opts.eps);
+  a.num_tokens = n;
+  a.q_row_stride = q.stride(0) * item;
+  a.k_row_stride = k.stride(0) * item;
+  a.v_row_stride = v.stride(0) * item;
+  a.q_out_row_stride = q_out.stride(0) * item;
+  a.cache_row_stride = k_cache.stride(0) * item;
+  a.num_slots = k_cache.size(0);
+  const c10::cuda::CUDAGuard guard(q.device());
+  CheckStatus(yl_qkv_norm_rope_store(&a, CurrentStream(q)), "yl_qkv_norm_rope_store");
+}
+
 DistributedInfo &GetDistributedInfo() {
   static DistributedInfo instance(0, 1);
   return instance;
@@ -187,6 +261,18 @@ void MHAKVCache::StoreKVAllLayers(torch::Tensor k, torch::Tensor v, torch::Tenso
   if (n == 0) return;
   RuntimeCheck(k.size(0) == m_num_layers_, "MHAKVCache::StoreKVAllLayers: k must hold every layer");
   StoreKVCacheLayers(k.view({m_num_layers_, n, -1}), v.view({m_num_layers_, n, -1}), m_k_rows_, m_v_rows_, loc);
+}
+
+torch::Tensor MHAKVCache::StoreKVNormRope(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor loc,
+                                          int layer_id, const QKNormRope &opts, std::optional<torch::Tensor> q_out) {
+  RuntimeCheck(layer_id >= 0 && layer_id < m_num_layers_, "MHAKVCache::StoreKVNormRope: layer_id out of range");
+  RuntimeCheck(loc.dim() == 1, "MHAKVCache::StoreKVNormRope: loc must be [N]");
+  const int64_t n = loc.size(0);
+  const auto heads = [&](const torch::Tensor &t) { return t.dim() == 3 ? t : t.view({n, -1, m_head_dim_}); };
+  torch::Tensor qh = heads(q), kh = heads(k), vh = heads(v);
+  torch::Tensor out = q_out ? heads(*q_out) : torch::empty_like(qh, qh.options().memory_format(at::MemoryFormat::Contiguous));
+  QKNormRopeStoreKV(qh, kh, vh, m_k_rows_[layer_id], m_v_rows_[layer_id], loc, opts, out);
+  return out;
 }
 
 torch::Tensor MHAKVCache::KCache(int layer_id) { return m_buffer_[0][layer_id]; }

@@ -74,6 +74,26 @@ void Index(const torch::Tensor &indices, const torch::Tensor &weights, const tor
 }
 
 // ----------------------------------------------------------------------------
+// One layer's attention input, fused (see yl_qkv_norm_rope_store): per-head
+// RMSNorm of q and k (weights [D]; none given: no norm), rotary embedding from
+// cos_sin_cache [max_position, D] fp32 by positions [N] (none: no rotation),
+// q written to q_out, k/v stored into the pool rows k_cache/v_cache [S, Hk*D]
+// at indices.  q [N, Hq, D], k/v [N, Hk, D], bf16 or fp16, token rows may be
+// strided.  The norm is flashinfer::norm::QKRMSNorm's (src/layers/rsm_norm.cu:49).
+// ----------------------------------------------------------------------------
+struct QKNormRope {
+  std::optional<torch::Tensor> q_weight;
+  std::optional<torch::Tensor> k_weight;
+  double eps{1e-6};
+  std::optional<torch::Tensor> cos_sin_cache;
+  std::optional<torch::Tensor> positions;
+  bool interleaved{false};
+};
+void QKNormRopeStoreKV(const torch::Tensor &q, const torch::Tensor &k, const torch::Tensor &v,
+                       const torch::Tensor &k_cache, const torch::Tensor &v_cache, const torch::Tensor &indices,
+                       const QKNormRope &opts, const torch::Tensor &q_out);
+
+// ----------------------------------------------------------------------------
 // Tensor-parallel rank info (only the head split uses it)
 // ----------------------------------------------------------------------------
 class DistributedInfo {
@@ -122,6 +142,10 @@ class MHAKVCache : public BaseKVCache {
   void StoreKV(torch::Tensor k, torch::Tensor v, torch::Tensor loc, int layer_id) override;
   // All layers at once: k, v [L, N, H_local * D] (or [L, N, H_local, D]).
   void StoreKVAllLayers(torch::Tensor k, torch::Tensor v, torch::Tensor loc);
+  // Q/K norm + rotary embedding + store of one layer (QKNormRopeStoreKV on
+  // this layer's pool rows); returns q_out ([N, Hq, D], a new tensor unless given).
+  torch::Tensor StoreKVNormRope(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor loc, int layer_id,
+                                const QKNormRope &opts, std::optional<torch::Tensor> q_out = std::nullopt);
 
   torch::Tensor KCache(int layer_id) override;
   torch::Tensor VCache(int layer_id) override;

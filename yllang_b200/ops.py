@@ -244,3 +244,89 @@ def gather_rows(indices: torch.Tensor, table: torch.Tensor, out: torch.Tensor | 
     a.error_word = error_word.data_ptr() if error_word is not None else None
     _abi.check(_abi.gather_rows_raw(a, _stream(stream, table.device)))
     return out
+
+
+def rope_cos_sin_cache(max_position: int, head_dim: int, theta: float = 1e6,
+                       device: torch.device | str = "cpu") -> torch.Tensor:
+    """[max_position, head_dim] fp32: head_dim / 2 cosines then head_dim / 2
+    sines of p * theta^(-2j / head_dim) (the model config's rope_theta,
+    src/models/model_config.cpp:38; 1e6 for Qwen3)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    angles = torch.arange(max_position, dtype=torch.float64)[:, None] * inv_freq[None, :]
+    return torch.cat([angles.cos(), angles.sin()], dim=1).to(torch.float32).to(device).contiguous()
+
+
+def _heads(t: torch.Tensor, name: str) -> tuple[int, int]:
+    _check(t.dim() == 3 and t.stride(2) == 1 and t.stride(1) == t.shape[2], f"{name} must be [N, heads, head_dim] "
+           "with contiguous heads")
+    return t.shape[1], t.shape[2]
+
+
+def qkv_norm_rope_store(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                        v_cache: torch.Tensor, slots: torch.Tensor, *, q_weight: torch.Tensor | None = None,
+                        k_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                        cos_sin_cache: torch.Tensor | None = None, positions: torch.Tensor | None = None,
+                        interleaved: bool = False, q_out: torch.Tensor | None = None,
+                        error_word: torch.Tensor | None = None,
+                        stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """One layer's attention input in one launch: per-head RMSNorm of q and k
+    (weights [head_dim]; None skips it), rotary embedding by positions from
+    cos_sin_cache (None skips it), then q written to q_out (default: a new
+    tensor; q itself for in place) and k, v stored into the pool rows
+    k_cache[slots[i]], v_cache[slots[i]].
+
+    q [N, Hq, D], k/v [N, Hk, D] (token rows may be strided, e.g. views of
+    one fused QKV projection); k_cache/v_cache [S, Hk * D] pool rows; slots
+    and positions int32 or int64 [N].  Returns q_out."""
+    Hq, D = _heads(q, "q")
+    Hk, Dk = _heads(k, "k")
+    _check(Dk == D and tuple(v.shape) == tuple(k.shape) and v.stride(2) == 1 and v.stride(1) == D,
+           "k and v must be [N, Hk, head_dim] with the head_dim of q")
+    N = q.shape[0]
+    _check(k.shape[0] == N and slots.dim() == 1 and slots.shape[0] == N, "q, k, v and slots must have N rows")
+    _check(q.dtype in (torch.bfloat16, torch.float16), "q/k/v must be bf16 or fp16")
+    for name, t in (("k", k), ("v", v), ("k_cache", k_cache), ("v_cache", v_cache)):
+        _check(t.dtype == q.dtype and t.device == q.device, f"{name} dtype/device must match q")
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        _check(t.dim() == 2 and t.shape[1] == Hk * D and t.stride(1) == 1, f"{name} must be [S, {Hk * D}] pool rows")
+    _check(k_cache.shape == v_cache.shape and k_cache.stride(0) == v_cache.stride(0),
+           "k_cache and v_cache must share shape and row stride")
+    _check(q.is_cuda, "q must be a CUDA tensor")
+    _check(slots.dtype in (torch.int32, torch.int64) and slots.device == q.device and (slots.stride(0) == 1 or N <= 1),
+           "slots must be contiguous int32/int64 on q's device")
+    for name, w in (("q_weight", q_weight), ("k_weight", k_weight)):
+        _check(w is None or (w.shape == (D,) and w.dtype == q.dtype and w.device == q.device and w.is_contiguous()),
+               f"{name} must be [{D}] of q's dtype and device")
+    if cos_sin_cache is not None:
+        _check(cos_sin_cache.dim() == 2 and cos_sin_cache.shape[1] == D and cos_sin_cache.dtype == torch.float32
+               and cos_sin_cache.is_contiguous() and cos_sin_cache.device == q.device,
+               f"cos_sin_cache must be contiguous fp32 [max_position, {D}] on q's device")
+        _check(positions is not None and positions.dim() == 1 and positions.shape[0] == N
+               and positions.dtype in (torch.int32, torch.int64) and positions.device == q.device
+               and (positions.stride(0) == 1 or N <= 1), "positions must be contiguous int32/int64 [N]")
+    if q_out is None:
+        q_out = torch.empty(N, Hq, D, dtype=q.dtype, device=q.device)
+    _check(q_out.shape == q.shape and q_out.dtype == q.dtype and q_out.stride(2) == 1 and q_out.stride(1) == D,
+           "q_out must be [N, Hq, head_dim] like q")
+    item = q.element_size()
+    a = _abi.QkvStoreArgs()
+    a.q, a.k, a.v, a.q_out = q.data_ptr(), k.data_ptr(), v.data_ptr(), q_out.data_ptr()
+    a.k_cache, a.v_cache, a.slots = k_cache.data_ptr(), v_cache.data_ptr(), slots.data_ptr()
+    a.q_weight = q_weight.data_ptr() if q_weight is not None else None
+    a.k_weight = k_weight.data_ptr() if k_weight is not None else None
+    if cos_sin_cache is not None:
+        a.cos_sin_cache, a.positions = cos_sin_cache.data_ptr(), positions.data_ptr()
+        a.position_is_int64 = int(positions.dtype == torch.int64)
+        a.max_position = cos_sin_cache.shape[0]
+    a.dtype = _abi.YL_DTYPE_BF16 if q.dtype == torch.bfloat16 else _abi.YL_DTYPE_F16
+    a.slot_is_int64 = int(slots.dtype == torch.int64)
+    a.rope_interleaved = int(bool(interleaved))
+    a.num_q_heads, a.num_kv_heads, a.head_dim, a.eps = Hq, Hk, D, float(eps)
+    a.num_tokens = N
+    a.q_row_stride, a.k_row_stride, a.v_row_stride = q.stride(0) * item, k.stride(0) * item, v.stride(0) * item
+    a.q_out_row_stride = q_out.stride(0) * item
+    a.cache_row_stride = k_cache.stride(0) * item
+    a.num_slots = k_cache.shape[0]
+    a.error_word = error_word.data_ptr() if error_word is not None else None
+    _abi.check(_abi.qkv_store_raw(a, _stream(stream, q.device)))
+    return q_out
