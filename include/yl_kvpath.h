@@ -71,6 +71,8 @@ typedef enum yl_status {
 #define YL_DEVERR_TIMEOUT         0x200u /* store: a bulk copy did not complete within 2 s    */
 #define YL_DEVERR_INDEX_RANGE     0x400u /* gather: index outside [-1, num_rows)              */
 #define YL_DEVERR_POSITION_RANGE  0x800u /* qkv store: position outside [0, max_position)     */
+#define YL_DEVERR_POOL_EMPTY      0x1000u /* reserve: fewer free pages than the batch needs  */
+#define YL_DEVERR_POOL_OVERFLOW   0x2000u /* release: more pages than the free list holds    */
 
 /*
  * Store (replaces yllang::StoreKVCache<kElementSize>,
@@ -287,6 +289,65 @@ typedef struct yl_qkv_store_args {
 } yl_qkv_store_args;
 
 YL_API int yl_qkv_norm_rope_store(const yl_qkv_store_args *args, cudaStream_t stream);
+
+/*
+ * Device page allocator: KVCacheManager's free-page list
+ * (src/include/kvcache/cache_manager.h:105-131, AllocateIndices) and page
+ * table (WritePageTable, :148-155) kept on the device, so the page ids the
+ * index build reads never cross to the host.
+ *
+ * The pool: free_pages[0, *free_count) are the free page ids, a stack whose
+ * top is the end.  Reserve gives the sequences of a batch, in batch order,
+ * the pages they lack, each taking the current tail of the list in order
+ * (AllocateIndices returns m_pages_.slice(0, -size), cache_manager.h:121-123,
+ * the list keeping its head), and writes them into the sequences' page-table
+ * rows after the pages already there: sequence i holds ceil(prior_len[i] /
+ * page_size) pages and needs ceil((prior_len[i] + new_len[i]) / page_size).
+ * Release appends the pages of the given rows (ceil(num_tokens[r] /
+ * page_size) each, in row order) to the list and sets those table entries to
+ * -1.  Both are all-or-nothing: any bad input (negative length, row outside
+ * the table, more pages than a row holds, a page id outside [0, capacity))
+ * or a pool that cannot satisfy the call sets an error bit and changes
+ * nothing.  One CTA runs each call; calls on one stream are ordered, calls on
+ * different streams on one pool race.  No counterpart kernel in the
+ * reference, whose allocator is host code.
+ */
+typedef struct yl_page_pool {
+  int32_t *free_pages;        /* [capacity] free page ids                          */
+  int32_t *free_count;        /* one int32 on the device                           */
+  int64_t capacity;           /* pages in the pool = entries of free_pages         */
+} yl_page_pool;
+
+typedef struct yl_reserve_args {
+  yl_page_pool pool;
+  int32_t *page_table;        /* [num_table_rows, page_table_stride] int32         */
+  const int32_t *prior_len;   /* [batch_size] tokens already in the row's pages    */
+  const int32_t *new_len;     /* [batch_size] tokens this step adds                */
+  const int32_t *table_index; /* [batch_size] row of each sequence; NULL: row i    */
+  int64_t page_table_stride;
+  int32_t num_table_rows;
+  int32_t max_pages_per_row;
+  int32_t page_size;
+  int32_t batch_size;
+  uint32_t *error_word;
+} yl_reserve_args;
+
+YL_API int yl_reserve_pages(const yl_reserve_args *args, cudaStream_t stream);
+
+typedef struct yl_release_args {
+  yl_page_pool pool;
+  int32_t *page_table;
+  const int32_t *rows;        /* [num_release] rows to free                        */
+  const int32_t *num_tokens;  /* [num_release] tokens each row holds               */
+  int64_t page_table_stride;
+  int32_t num_table_rows;
+  int32_t max_pages_per_row;
+  int32_t page_size;
+  int32_t num_release;
+  uint32_t *error_word;
+} yl_release_args;
+
+YL_API int yl_release_pages(const yl_release_args *args, cudaStream_t stream);
 
 /* Human-readable name of a yl_status value (static storage). */
 YL_API const char *yl_status_string(int status);

@@ -39,6 +39,8 @@ INDPTR_OVERFLOW = 0x40
 TABLE_ROW = 0x80
 INDEX_RANGE = 0x400
 POSITION_RANGE = 0x800
+POOL_EMPTY = 0x1000
+POOL_OVERFLOW = 0x2000
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -68,6 +70,12 @@ def lib() -> ctypes.CDLL:
         L.oracle_build_index.argtypes = [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp,
                                          _vp, ctypes.c_int, _i64, _i64, _vp]
         L.oracle_max_threads.restype = ctypes.c_int
+        L.oracle_reserve_pages.restype = ctypes.c_uint32
+        L.oracle_reserve_pages.argtypes = [_vp, _vp, _i64, _vp, _i64, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp,
+                                           ctypes.c_int32, ctypes.c_int32]
+        L.oracle_release_pages.restype = ctypes.c_uint32
+        L.oracle_release_pages.argtypes = [_vp, _vp, _i64, _vp, _i64, ctypes.c_int32, ctypes.c_int32, _vp, _vp,
+                                           ctypes.c_int32, ctypes.c_int32]
         L.oracle_gather_rows.restype = _i64
         L.oracle_gather_rows.argtypes = [_vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _vp]
         _lib = L
@@ -161,6 +169,39 @@ def gather(indices: np.ndarray, table: np.ndarray, num_rows: int | None = None) 
                                  table.shape[1] * table.itemsize, table.strides[0], out.strides[0],
                                  table.shape[0] if num_rows is None else num_rows, ctypes.addressof(err))
     return out, int(err.value)
+
+
+class PagePool:
+    """The free-page list of KVCacheManager (cache_manager.h:105-131) on the
+    host: free_pages[:count] are free, the top is the end.  reserve/release
+    update it and the int32 page table in place and return error bits."""
+
+    def __init__(self, num_pages: int, free_pages: np.ndarray | None = None):
+        self.capacity = num_pages
+        self.free_pages = (np.arange(num_pages, dtype=np.int32) if free_pages is None
+                           else np.ascontiguousarray(free_pages, np.int32).copy())
+        self.count = np.array([self.free_pages.shape[0]], np.int32)
+        self.free_pages = np.concatenate([self.free_pages, np.full(num_pages - self.free_pages.shape[0], -1,
+                                                                   np.int32)])
+
+    def reserve(self, table: np.ndarray, prior, new, page_size: int, table_index=None) -> int:
+        assert table.dtype == np.int32 and table.flags.c_contiguous
+        prior = np.ascontiguousarray(prior, np.int32)
+        new = np.ascontiguousarray(new, np.int32)
+        ti = None if table_index is None else np.ascontiguousarray(table_index, np.int32)
+        return int(lib().oracle_reserve_pages(_ptr(self.free_pages), _ptr(self.count), self.capacity, _ptr(table),
+                                              table.shape[1], table.shape[0], table.shape[1], _ptr(prior), _ptr(new),
+                                              None if ti is None else _ptr(ti), page_size, prior.shape[0]))
+
+    def release(self, table: np.ndarray, rows, num_tokens, page_size: int) -> int:
+        rows = np.ascontiguousarray(rows, np.int32)
+        toks = np.ascontiguousarray(num_tokens, np.int32)
+        return int(lib().oracle_release_pages(_ptr(self.free_pages), _ptr(self.count), self.capacity, _ptr(table),
+                                              table.shape[1], table.shape[0], table.shape[1], _ptr(rows), _ptr(toks),
+                                              page_size, rows.shape[0]))
+
+    def free_list(self) -> np.ndarray:
+        return self.free_pages[:int(self.count[0])].copy()
 
 
 def round_to(x: np.ndarray, dtype: str) -> np.ndarray:

@@ -233,6 +233,88 @@ int64_t oracle_gather_rows(const uint8_t *table, uint8_t *out, const void *indic
   return copied;
 }
 
+/*
+ * Page allocator, request by request as KVCacheManager::AllocateIndices runs
+ * (src/include/kvcache/cache_manager.h:119-131): a request lacking `size`
+ * pages takes the last `size` entries of the free list, in order, and the
+ * list keeps the rest (the reference keeps slice(0, size), a defect); the
+ * pages go into the request's page-table row after the pages it holds
+ * (WritePageTable, :148-155, meant for the page table).  All-or-nothing:
+ * returns error bits and changes nothing when any request is invalid or the
+ * list is short.  Bits as in yl_kvpath.h.
+ */
+#define O_NEGATIVE_LEN 0x20u
+#define O_TABLE_ROW 0x80u
+#define O_ROW_OVERFLOW 0x4u
+#define O_PAGE_RANGE 0x2u
+#define O_POOL_EMPTY 0x1000u
+#define O_POOL_OVERFLOW 0x2000u
+
+static int64_t o_pages_for(int64_t tokens, int32_t ps) { return (tokens + ps - 1) / ps; }
+
+uint32_t oracle_reserve_pages(int32_t *free_pages, int32_t *free_count, int64_t capacity, int32_t *table,
+                              int64_t stride, int32_t num_rows, int32_t max_pages, const int32_t *prior,
+                              const int32_t *fresh, const int32_t *table_index, int32_t page_size, int32_t batch) {
+  uint32_t err = 0;
+  int64_t total = 0;
+  for (int32_t i = 0; i < batch; ++i) {
+    const int32_t row = table_index ? table_index[i] : i;
+    if (prior[i] < 0 || fresh[i] < 0) { err |= O_NEGATIVE_LEN; continue; }
+    if (row < 0 || row >= num_rows) { err |= O_TABLE_ROW; continue; }
+    const int64_t need = o_pages_for((int64_t)prior[i] + fresh[i], page_size);
+    if (need > max_pages) { err |= O_ROW_OVERFLOW; continue; }
+    total += need - o_pages_for(prior[i], page_size);
+  }
+  const int64_t n = *free_count;
+  if (!err && (n < 0 || n > capacity || total > n)) err |= O_POOL_EMPTY;
+  for (int64_t k = n - total; !err && k < n; ++k)
+    if (free_pages[k] < 0 || free_pages[k] >= capacity) err |= O_PAGE_RANGE;
+  if (err) return err;
+  int64_t top = n;
+  for (int32_t i = 0; i < batch; ++i) {
+    const int32_t row = table_index ? table_index[i] : i;
+    const int64_t held = o_pages_for(prior[i], page_size);
+    const int64_t lack = o_pages_for((int64_t)prior[i] + fresh[i], page_size) - held;
+    for (int64_t j = 0; j < lack; ++j) table[row * stride + held + j] = free_pages[top - lack + j];
+    top -= lack;
+  }
+  *free_count = (int32_t)top;
+  return 0;
+}
+
+/* Release: rows in order append their ceil(tokens / page_size) pages to the
+ * free list and clear those table entries to -1; all-or-nothing. */
+uint32_t oracle_release_pages(int32_t *free_pages, int32_t *free_count, int64_t capacity, int32_t *table,
+                              int64_t stride, int32_t num_rows, int32_t max_pages, const int32_t *rows,
+                              const int32_t *num_tokens, int32_t page_size, int32_t count) {
+  uint32_t err = 0;
+  int64_t total = 0;
+  for (int32_t r = 0; r < count; ++r) {
+    if (num_tokens[r] < 0) { err |= O_NEGATIVE_LEN; continue; }
+    if (rows[r] < 0 || rows[r] >= num_rows) { err |= O_TABLE_ROW; continue; }
+    const int64_t c = o_pages_for(num_tokens[r], page_size);
+    if (c > max_pages) { err |= O_ROW_OVERFLOW; continue; }
+    for (int64_t j = 0; j < c; ++j) {
+      const int32_t id = table[rows[r] * stride + j];
+      if (id < 0 || id >= capacity) err |= O_PAGE_RANGE;
+    }
+    total += c;
+  }
+  const int64_t n = *free_count;
+  if (!err && (n < 0 || n + total > capacity)) err |= O_POOL_OVERFLOW;
+  if (err) return err;
+  int64_t top = n;
+  for (int32_t r = 0; r < count; ++r) {
+    const int64_t c = o_pages_for(num_tokens[r], page_size);
+    for (int64_t j = 0; j < c; ++j) {
+      free_pages[top++] = table[rows[r] * stride + j];
+      table[rows[r] * stride + j] = -1;
+    }
+  }
+  *free_count = (int32_t)top;
+  return 0;
+}
+
 /* Host threads available to this process (online processors). */
 int oracle_max_threads(void) {
   const long n = sysconf(_SC_NPROCESSORS_ONLN);

@@ -49,7 +49,8 @@ def _c_layout(tmp_path, struct, fields):
 
 @pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs),
                                         ("yl_step_args", _abi.StepArgs), ("yl_gather_args", _abi.GatherArgs),
-                                        ("yl_qkv_store_args", _abi.QkvStoreArgs)])
+                                        ("yl_qkv_store_args", _abi.QkvStoreArgs), ("yl_page_pool", _abi.PagePool),
+                                        ("yl_reserve_args", _abi.ReserveArgs), ("yl_release_args", _abi.ReleaseArgs)])
 def test_struct_layout_matches_header(tmp_path, struct, cls):
     names = [f for f, _ in cls._fields_]
     c = _c_layout(tmp_path, struct, names)
@@ -193,6 +194,52 @@ def test_qkv_store_rejects_bad_arguments_on_host(kw, status):
 def test_qkv_store_zero_tokens_is_noop_without_device():
     assert _abi.qkv_store_raw(_qkv(num_tokens=0, q=0, k=0, v=0, slots=0), None) == _abi.YL_OK
     assert yl.lib().yl_qkv_norm_rope_store(None, None) == _abi.YL_ERR_NULL_ARG
+
+
+def _pool_args(cls, **kw):
+    a = cls()
+    a.pool = _abi.PagePool(0x1000, 0x2000, 64)
+    base = dict(page_table=0x3000, page_table_stride=8, num_table_rows=4, max_pages_per_row=8, page_size=16)
+    if cls is _abi.ReserveArgs:
+        base.update(prior_len=0x4000, new_len=0x5000, batch_size=4)
+    else:
+        base.update(rows=0x4000, num_tokens=0x5000, num_release=2)
+    for k, v in kw.items():
+        if k.startswith("pool_"):
+            setattr(a.pool, k[5:], v)
+        else:
+            base[k] = v
+    for k, v in base.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kind", ["reserve", "release"])
+@pytest.mark.parametrize("kw,status", [
+    (dict(pool_free_pages=0), _abi.YL_ERR_NULL_ARG),
+    (dict(pool_capacity=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(pool_capacity=1 << 31), _abi.YL_ERR_BAD_SIZE),
+    (dict(pool_free_count=0x2002), _abi.YL_ERR_ALIGNMENT),
+    (dict(page_table=0), _abi.YL_ERR_NULL_ARG),
+    (dict(page_size=0), _abi.YL_ERR_BAD_SIZE),
+    (dict(page_table_stride=4), _abi.YL_ERR_BAD_SIZE),
+    (dict(page_table=0x3002), _abi.YL_ERR_ALIGNMENT),
+])
+def test_page_pool_rejects_bad_arguments_on_host(kind, kw, status):
+    cls, raw, name = ((_abi.ReserveArgs, _abi.reserve_pages_raw, "yl_reserve_pages") if kind == "reserve" else
+                      (_abi.ReleaseArgs, _abi.release_pages_raw, "yl_release_pages"))
+    assert raw(_pool_args(cls, **kw), None) == status
+    assert _abi.last_error().startswith(name)
+
+
+def test_page_pool_empty_calls_are_noops_without_device():
+    assert _abi.reserve_pages_raw(_pool_args(_abi.ReserveArgs, batch_size=0, pool_free_pages=0), None) == _abi.YL_OK
+    assert _abi.release_pages_raw(_pool_args(_abi.ReleaseArgs, num_release=0, page_table=0), None) == _abi.YL_OK
+    assert _abi.reserve_pages_raw(_pool_args(_abi.ReserveArgs, batch_size=-1), None) == _abi.YL_ERR_BAD_SIZE
+    assert _abi.reserve_pages_raw(_pool_args(_abi.ReserveArgs, batch_size=5), None) == _abi.YL_ERR_BAD_SIZE
+    assert _abi.reserve_pages_raw(_pool_args(_abi.ReserveArgs, new_len=0), None) == _abi.YL_ERR_NULL_ARG
+    assert yl.lib().yl_reserve_pages(None, None) == _abi.YL_ERR_NULL_ARG
+    assert yl.lib().yl_release_pages(None, None) == _abi.YL_ERR_NULL_ARG
 
 
 def test_status_strings():

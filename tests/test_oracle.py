@@ -266,3 +266,101 @@ def test_qkv_oracle_error_bits():
     assert np.isnan(q_out[1]).all() and not np.isnan(q_out[[0, 2, 3, 4, 5]]).any()
     written = {int(s) for i, s in enumerate(slots) if i not in (1, 2, 3)}
     assert {int(s) for s in np.nonzero(vc.any(axis=(1, 2)))[0]} == written
+
+
+def _reference_allocator(P, steps, ps, W):
+    """A literal restatement of the reference's AllocateIndices on a Python
+    list (cache_manager.h:119-131: return the tail slice, keep the head) plus
+    the page-table writes, request by request."""
+    free = list(range(P))
+    table = [[-1] * W for _ in range(len(steps[0][1]))]
+    for op, a, b in steps:
+        if op == "reserve":
+            for i, (prior, new) in enumerate(zip(a, b)):
+                held, need = -(-prior // ps), -(-(prior + new) // ps)
+                size = need - held
+                if size:
+                    got, free = free[len(free) - size:], free[:len(free) - size]
+                    table[i][held:need] = got
+        else:
+            for row, toks in zip(a, b):
+                c = -(-toks // ps)
+                free += table[row][:c]
+                table[row][:c] = [-1] * c
+    return free, table
+
+
+@pytest.mark.parametrize("ps", [1, 16])
+def test_page_pool_oracle_matches_list_restatement(ps):
+    rng = np.random.default_rng(ps)
+    B, W, P = 12, 64, 800
+    lens = np.zeros(B, np.int64)
+    steps = []
+    for _ in range(30):
+        if rng.random() < 0.3:
+            rows = rng.choice(B, size=3, replace=False)
+            steps.append(("release", rows.tolist(), lens[rows].tolist()))
+            lens[rows] = 0
+        else:
+            new = rng.integers(0, 3 * ps, B)
+            new = np.minimum(new, W * ps - lens)
+            steps.append(("reserve", lens.tolist(), new.tolist()))
+            lens += new
+    pool = orc.PagePool(P)
+    table = np.full((B, W), -1, np.int32)
+    for op, a, b in steps:
+        err = pool.reserve(table, a, b, ps) if op == "reserve" else pool.release(table, a, b, ps)
+        assert err == 0
+    free, want = _reference_allocator(P, [(op, a, b) if op == "release" else (op, a, b) for op, a, b in steps], ps, W)
+    assert pool.free_list().tolist() == free
+    assert table.tolist() == want
+
+
+def test_page_pool_oracle_is_all_or_nothing():
+    pool = orc.PagePool(10)
+    table = np.full((3, 8), -1, np.int32)
+    assert pool.reserve(table, [0, 0], [16, 30], 4) == orc.POOL_EMPTY  # 4 + 8 pages > 10 free
+    assert pool.reserve(table, [0, 0], [16, 33], 4) == 0x4  # second row would need 9 > 8 pages
+    assert pool.reserve(table, [0, -1], [4, 4], 4) == 0x20
+    assert pool.reserve(table, [0, 0], [4, 4], 4, table_index=[0, 3]) == 0x80
+    assert (table == -1).all() and pool.count[0] == 10
+    assert pool.reserve(table, [0, 0], [8, 4], 4) == 0
+    # request 0 takes the tail [8, 9], request 1 the next tail [7]
+    assert table[0, :2].tolist() == [8, 9] and table[1, :1].tolist() == [7] and pool.count[0] == 7
+    assert pool.release(table, [0, 0], [8, 8], 4) == orc.POOL_OVERFLOW and pool.count[0] == 7  # 7 + 4 > 10
+    assert pool.release(table, [0], [8], 4) == 0 and pool.free_list().tolist() == list(range(7)) + [8, 9]
+    assert pool.release(table, [1], [4], 4) == 0 and pool.free_list().tolist() == list(range(7)) + [8, 9, 7]
+    bad = np.array([[5, 11, -1, -1, -1, -1, -1, -1]] * 3, np.int32)
+    assert pool.release(bad, [0], [8], 4) == 0x2 and pool.count[0] == 10  # page id 11 outside the pool
+
+
+def test_host_kvcache_manager_matches_page_pool_oracle():
+    """The C++ front end's host KVCacheManager (Reserve / Release, one request
+    at a time) and the oracle give the same page table and free list."""
+    import torch
+
+    import yllang_b200 as yl
+
+    C = yl.load_extension()
+    P, R, W, ps = 300, 6, 32, 16
+    m = C.KVCacheManager(P, R, W, ps, "cpu")
+    rows = [m.AllocateTableSlot() for _ in range(R)]
+    pool = orc.PagePool(P)
+    table = np.full((R, W), -1, np.int32)
+    rng = np.random.default_rng(9)
+    lens = np.zeros(R, np.int64)
+    for step in range(25):
+        if step % 7 == 6:
+            r = int(rng.integers(0, R))
+            m.Release(rows[r])
+            assert pool.release(table, [rows[r]], [int(lens[r])], ps) == 0
+            rows[r] = m.AllocateTableSlot()
+            lens[r] = 0
+            continue
+        new = np.minimum(rng.integers(0, 40, R), W * ps - lens)
+        for i in range(R):
+            m.Reserve(rows[i], int(lens[i] + new[i]))
+        assert pool.reserve(table, lens, new, ps, table_index=np.array(rows)) == 0
+        lens += new
+    assert np.array_equal(m.HostPageTable().numpy(), table)
+    assert m.RemainingPageCount() == int(pool.count[0])

@@ -12,6 +12,10 @@ rotation a*c - b*s mixes two such values, so the bound is 2 ulp of the head
 row's largest magnitude per element, with at most 1 % of elements differing.
 Without rotation a single rounding separates them: at most 1 ulp per element.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 import torch
@@ -105,6 +109,23 @@ def test_fused_matches_oracle(cuda, D, dtype, interleaved):
     untouched = torch.ones(S, dtype=torch.bool)
     untouched[slots.cpu()] = False
     assert torch.equal(k_cache.cpu()[untouched], want_k[untouched])
+
+
+@pytest.mark.parametrize("Hq,Hk,D", [(32, 8, 128), (12, 3, 128), (16, 4, 256), (8, 1, 64)])
+def test_fused_large_batch_matches_oracle(cuda, Hq, Hk, D):
+    """8192 tokens: enough chunks for the 8-head (4 at head_dim 256) chunk
+    kernel, including partial chunks (12 Q heads, 3 KV heads)."""
+    N, S = 8192, 16384
+    q, k, v, qw, kw, k_cache, v_cache, slots, positions = _case(cuda, N, Hq, Hk, D, torch.bfloat16, S, seed=Hq + D)
+    cs = yl.rope_cos_sin_cache(4096, D, theta=1e6, device=cuda)
+    want_q, want_k, want_v, _ = _oracle(q, k, v, k_cache, v_cache, slots, qw, kw, 1e-6, cs, positions, False,
+                                        torch.bfloat16)
+    q_out = yl.qkv_norm_rope_store(q, k, v, k_cache, v_cache, slots, q_weight=qw, k_weight=kw, eps=1e-6,
+                                   cos_sin_cache=cs, positions=positions)
+    torch.cuda.synchronize()
+    assert_ulp_close(q_out, want_q, D)
+    assert_ulp_close(k_cache, want_k, D)
+    assert torch.equal(v_cache.cpu(), want_v)
 
 
 @pytest.mark.parametrize("norm,rope", [(False, False), (True, False), (False, True)])
@@ -268,3 +289,14 @@ def test_cpp_front_end_store_kv_norm_rope(cuda):
     assert float(cache.KCache(0).abs().sum()) == 0.0
     with pytest.raises(C.PanicError):
         cache.StoreKVNormRope(q.float(), k, v, slots, 1, opts)
+
+
+@pytest.mark.parametrize("engine", ["register", "tma"])
+def test_fused_engines_match(cuda, engine):
+    """Every case above through one engine only: the register kernels (2- or
+    8-head chunks) or the TMA-staged kernel, which otherwise only large
+    batches reach (the engine is read once per process: run in a child)."""
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.abspath(__file__), "-k", "not engines_match"],
+                       env=dict(os.environ, YL_QKV_ENGINE=engine), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

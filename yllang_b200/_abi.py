@@ -32,6 +32,8 @@ DEVERR_TOKEN_COUNT = 0x100
 DEVERR_TIMEOUT = 0x200
 DEVERR_INDEX_RANGE = 0x400
 DEVERR_POSITION_RANGE = 0x800
+DEVERR_POOL_EMPTY = 0x1000
+DEVERR_POOL_OVERFLOW = 0x2000
 
 ABI_VERSION = 1
 
@@ -151,9 +153,50 @@ class QkvStoreArgs(ctypes.Structure):
 
 YL_DTYPE_BF16, YL_DTYPE_F16 = 0, 1
 
+
+class PagePool(ctypes.Structure):
+    """struct yl_page_pool."""
+
+    _fields_ = [("free_pages", _vp), ("free_count", _vp), ("capacity", _i64)]
+
+
+class ReserveArgs(ctypes.Structure):
+    """struct yl_reserve_args."""
+
+    _fields_ = [
+        ("pool", PagePool),
+        ("page_table", _vp),
+        ("prior_len", _vp),
+        ("new_len", _vp),
+        ("table_index", _vp),
+        ("page_table_stride", _i64),
+        ("num_table_rows", _i32),
+        ("max_pages_per_row", _i32),
+        ("page_size", _i32),
+        ("batch_size", _i32),
+        ("error_word", _vp),
+    ]
+
+
+class ReleaseArgs(ctypes.Structure):
+    """struct yl_release_args."""
+
+    _fields_ = [
+        ("pool", PagePool),
+        ("page_table", _vp),
+        ("rows", _vp),
+        ("num_tokens", _vp),
+        ("page_table_stride", _i64),
+        ("num_table_rows", _i32),
+        ("max_pages_per_row", _i32),
+        ("page_size", _i32),
+        ("num_release", _i32),
+        ("error_word", _vp),
+    ]
+
 # Every symbol include/yl_kvpath.h declares.
 EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_gather_rows", "yl_qkv_norm_rope_store",
-                    "yl_status_string", "yl_last_error", "yl_abi_version")
+                    "yl_reserve_pages", "yl_release_pages", "yl_status_string", "yl_last_error", "yl_abi_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -185,6 +228,10 @@ def lib() -> ctypes.CDLL:
         L.yl_gather_rows.argtypes = [ctypes.POINTER(GatherArgs), _vp]
         L.yl_qkv_norm_rope_store.restype = ctypes.c_int
         L.yl_qkv_norm_rope_store.argtypes = [ctypes.POINTER(QkvStoreArgs), _vp]
+        L.yl_reserve_pages.restype = ctypes.c_int
+        L.yl_reserve_pages.argtypes = [ctypes.POINTER(ReserveArgs), _vp]
+        L.yl_release_pages.restype = ctypes.c_int
+        L.yl_release_pages.argtypes = [ctypes.POINTER(ReleaseArgs), _vp]
         L.yl_status_string.restype = ctypes.c_char_p
         L.yl_status_string.argtypes = [ctypes.c_int]
         L.yl_last_error.restype = ctypes.c_char_p
@@ -228,3 +275,11 @@ def gather_rows_raw(args: GatherArgs, stream: int | None) -> int:
 
 def qkv_store_raw(args: QkvStoreArgs, stream: int | None) -> int:
     return lib().yl_qkv_norm_rope_store(ctypes.byref(args), stream)
+
+
+def reserve_pages_raw(args: ReserveArgs, stream: int | None) -> int:
+    return lib().yl_reserve_pages(ctypes.byref(args), stream)
+
+
+def release_pages_raw(args: ReleaseArgs, stream: int | None) -> int:
+    return lib().yl_release_pages(ctypes.byref(args), stream)

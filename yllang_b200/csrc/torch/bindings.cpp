@@ -36,6 +36,19 @@ PYBIND11_MODULE(_C, m) {
       py::arg("indices"), py::arg("weights"), py::arg("destination"),
       "destination[i] = weights[indices[i]] (the embedding lookup of yllang::Index)");
 
+  py::class_<DevicePagePool, std::shared_ptr<DevicePagePool>>(m, "DevicePagePool")
+      .def(py::init([](int64_t num_pages, const std::string &device) {
+             return std::make_shared<DevicePagePool>(num_pages, torch::Device(device));
+           }),
+           py::arg("num_pages"), py::arg("device") = "cuda")
+      .def("Reserve", &DevicePagePool::Reserve, py::arg("page_table"), py::arg("prior_len"), py::arg("new_len"),
+           py::arg("page_size"), py::arg("table_index") = py::none(), py::arg("error_word") = py::none())
+      .def("Release", &DevicePagePool::Release, py::arg("page_table"), py::arg("rows"), py::arg("num_tokens"),
+           py::arg("page_size"), py::arg("error_word") = py::none())
+      .def("FreeCount", &DevicePagePool::FreeCount)
+      .def("FreeList", &DevicePagePool::FreeList)
+      .def("Capacity", &DevicePagePool::Capacity);
+
   py::class_<QKNormRope>(m, "QKNormRope")
       .def(py::init<>())
       .def_readwrite("q_weight", &QKNormRope::q_weight)

@@ -215,6 +215,74 @@ void QKNormRopeStoreKV(const torch::Tensor &q, const torch::Tensor &k, const tor
   CheckStatus(yl_qkv_norm_rope_store(&a, CurrentStream(q)), "yl_qkv_norm_rope_store");
 }
 
+// ----------------------------------------------------------------------------
+DevicePagePool::DevicePagePool(int64_t num_pages, torch::Device device) : m_capacity_(num_pages), m_device_(device) {
+  RuntimeCheck(num_pages > 0 && num_pages <= INT32_MAX, "DevicePagePool: num_pages must be in [1, 2^31)");
+  RuntimeCheck(device.is_cuda(), "DevicePagePool: the pool lives on a CUDA device");
+  if (!m_device_.has_index()) m_device_ = torch::Device(torch::kCUDA, c10::cuda::current_device());
+  m_free_pages_ = torch::arange(num_pages, torch::dtype(torch::kInt32).device(device));
+  m_free_count_ = torch::full({1}, num_pages, torch::dtype(torch::kInt32).device(device));
+}
+
+namespace {
+const int32_t *Int32Vector(const torch::Tensor &t, int64_t n, const torch::Device &dev, const char *what) {
+  RuntimeCheck(t.dim() == 1 && t.size(0) == n && t.scalar_type() == torch::kInt32 && t.device() == dev &&
+                   (n <= 1 || t.stride(0) == 1),
+               std::string("DevicePagePool: ") + what + " must be contiguous int32 [n] on the pool's device");
+  return t.data_ptr<int32_t>();
+}
+}  // namespace
+
+void DevicePagePool::Reserve(const torch::Tensor &page_table, const torch::Tensor &prior_len,
+                             const torch::Tensor &new_len, int page_size,
+                             const std::optional<torch::Tensor> &table_index,
+                             const std::optional<torch::Tensor> &error_word) {
+  RuntimeCheck(page_table.dim() == 2 && page_table.scalar_type() == torch::kInt32 && page_table.stride(1) == 1 &&
+                   page_table.device() == m_device_,
+               "DevicePagePool::Reserve: page_table must be int32 [R, W] on the pool's device");
+  const int64_t B = prior_len.size(0);
+  yl_reserve_args a{};
+  a.pool = {m_free_pages_.data_ptr<int32_t>(), m_free_count_.data_ptr<int32_t>(), m_capacity_};
+  a.page_table = page_table.data_ptr<int32_t>();
+  a.prior_len = Int32Vector(prior_len, B, m_device_, "prior_len");
+  a.new_len = Int32Vector(new_len, B, m_device_, "new_len");
+  a.table_index = table_index ? Int32Vector(*table_index, B, m_device_, "table_index") : nullptr;
+  a.page_table_stride = page_table.stride(0);
+  a.num_table_rows = static_cast<int32_t>(page_table.size(0));
+  a.max_pages_per_row = static_cast<int32_t>(page_table.size(1));
+  a.page_size = page_size;
+  a.batch_size = static_cast<int32_t>(B);
+  a.error_word = error_word ? reinterpret_cast<uint32_t *>(error_word->data_ptr()) : nullptr;
+  const c10::cuda::CUDAGuard guard(m_device_);
+  CheckStatus(yl_reserve_pages(&a, c10::cuda::getCurrentCUDAStream(m_device_.index()).stream()), "yl_reserve_pages");
+}
+
+void DevicePagePool::Release(const torch::Tensor &page_table, const torch::Tensor &rows,
+                             const torch::Tensor &num_tokens, int page_size,
+                             const std::optional<torch::Tensor> &error_word) {
+  RuntimeCheck(page_table.dim() == 2 && page_table.scalar_type() == torch::kInt32 && page_table.stride(1) == 1 &&
+                   page_table.device() == m_device_,
+               "DevicePagePool::Release: page_table must be int32 [R, W] on the pool's device");
+  const int64_t R = rows.size(0);
+  yl_release_args a{};
+  a.pool = {m_free_pages_.data_ptr<int32_t>(), m_free_count_.data_ptr<int32_t>(), m_capacity_};
+  a.page_table = page_table.data_ptr<int32_t>();
+  a.rows = Int32Vector(rows, R, m_device_, "rows");
+  a.num_tokens = Int32Vector(num_tokens, R, m_device_, "num_tokens");
+  a.page_table_stride = page_table.stride(0);
+  a.num_table_rows = static_cast<int32_t>(page_table.size(0));
+  a.max_pages_per_row = static_cast<int32_t>(page_table.size(1));
+  a.page_size = page_size;
+  a.num_release = static_cast<int32_t>(R);
+  a.error_word = error_word ? reinterpret_cast<uint32_t *>(error_word->data_ptr()) : nullptr;
+  const c10::cuda::CUDAGuard guard(m_device_);
+  CheckStatus(yl_release_pages(&a, c10::cuda::getCurrentCUDAStream(m_device_.index()).stream()), "yl_release_pages");
+}
+
+int64_t DevicePagePool::FreeCount() const { return m_free_count_.item<int32_t>(); }
+
+torch::Tensor DevicePagePool::FreeList() const { return m_free_pages_.narrow(0, 0, FreeCount()).clone(); }
+
 DistributedInfo &GetDistributedInfo() {
   static DistributedInfo instance(0, 1);
   return instance;
@@ -355,9 +423,10 @@ KVCacheManager::KVCacheManager(int64_t num_pages, int64_t max_requests, int64_t 
   RuntimeCheck(num_pages > 0 && num_pages <= INT32_MAX && max_requests > 0 && max_pages_per_request > 0 &&
                    page_size > 0,
                "KVCacheManager: bad sizes");
+  // the free list is page ids 0..P-1 in order and allocation takes its tail
+  // (cache_manager.h:33-34, 121-123), the order the device pool keeps too
   m_free_pages_.resize(static_cast<size_t>(num_pages));
-  // lowest ids handed out first
-  for (int64_t i = 0; i < num_pages; ++i) m_free_pages_[static_cast<size_t>(i)] = static_cast<int32_t>(num_pages - 1 - i);
+  for (int64_t i = 0; i < num_pages; ++i) m_free_pages_[static_cast<size_t>(i)] = static_cast<int32_t>(i);
   m_free_rows_.resize(static_cast<size_t>(max_requests));
   for (int64_t i = 0; i < max_requests; ++i) m_free_rows_[static_cast<size_t>(i)] = max_requests - 1 - i;
   m_row_pages_.assign(static_cast<size_t>(max_requests), 0);
@@ -374,12 +443,12 @@ int64_t KVCacheManager::AllocateTableSlot() {
 
 torch::Tensor KVCacheManager::AllocatePages(int64_t n) {
   TORCH_CHECK(n >= 0 && static_cast<size_t>(n) <= m_free_pages_.size(), "not enough pages");
+  // the last n entries of the list, in order (AllocateIndices, cache_manager.h:121-123)
   auto out = torch::empty({n}, torch::dtype(torch::kInt32));
   auto *p = out.data_ptr<int32_t>();
-  for (int64_t i = 0; i < n; ++i) {
-    p[i] = m_free_pages_.back();
-    m_free_pages_.pop_back();
-  }
+  const size_t keep = m_free_pages_.size() - static_cast<size_t>(n);
+  for (int64_t i = 0; i < n; ++i) p[i] = m_free_pages_[keep + static_cast<size_t>(i)];
+  m_free_pages_.resize(keep);
   return out;
 }
 

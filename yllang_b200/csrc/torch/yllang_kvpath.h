@@ -244,6 +244,31 @@ class KVCacheManager {
   torch::Tensor m_page_table_;            // device int32 [R, W]
 };
 
+// The same free-page list and page-table updates on the device (see
+// yl_reserve_pages / yl_release_pages): the list starts as page ids
+// 0..num_pages-1, a request takes the tail of the list in order, released
+// pages are appended in row order, so a sequence of Reserve / Release calls
+// gives the page table KVCacheManager's Reserve / Release give.  Calls are
+// asynchronous on the current stream; FreeCount() reads the count back.
+class DevicePagePool {
+ public:
+  DevicePagePool(int64_t num_pages, torch::Device device);
+  void Reserve(const torch::Tensor &page_table, const torch::Tensor &prior_len, const torch::Tensor &new_len,
+               int page_size, const std::optional<torch::Tensor> &table_index = std::nullopt,
+               const std::optional<torch::Tensor> &error_word = std::nullopt);
+  void Release(const torch::Tensor &page_table, const torch::Tensor &rows, const torch::Tensor &num_tokens,
+               int page_size, const std::optional<torch::Tensor> &error_word = std::nullopt);
+  int64_t FreeCount() const;
+  torch::Tensor FreeList() const;  // device int32 [FreeCount()]
+  int64_t Capacity() const { return m_capacity_; }
+
+ private:
+  int64_t m_capacity_;
+  torch::Device m_device_;
+  torch::Tensor m_free_pages_;  // device int32 [capacity]
+  torch::Tensor m_free_count_;  // device int32 [1]
+};
+
 // One request in a batch: the reference Request's table_index, cached_len
 // and device_len (src/include/request/request.h:81-92).
 struct RequestSlot {

@@ -330,3 +330,72 @@ def qkv_norm_rope_store(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cac
     a.error_word = error_word.data_ptr() if error_word is not None else None
     _abi.check(_abi.qkv_store_raw(a, _stream(stream, q.device)))
     return q_out
+
+
+class DevicePagePool:
+    """KVCacheManager's free-page list kept on the device (yl_reserve_pages /
+    yl_release_pages): free_pages[:free_count] are the free page ids, the top
+    of the stack is the end.  The initial list is page ids 0..num_pages-1 in
+    order (the reference builds it with torch::range, cache_manager.h:33-34),
+    unless `free_pages` gives another order.  All methods are asynchronous on
+    the current stream except free_count()."""
+
+    def __init__(self, num_pages: int, device: torch.device | str = "cuda", free_pages: torch.Tensor | None = None):
+        _check(0 < num_pages < (1 << 31), "num_pages must be in [1, 2^31)")
+        self.capacity = int(num_pages)
+        self.device = torch.device(device)
+        self.free_pages = torch.full((num_pages,), -1, dtype=torch.int32, device=self.device)
+        init = torch.arange(num_pages, dtype=torch.int32) if free_pages is None else free_pages.to(torch.int32)
+        _check(init.dim() == 1 and init.shape[0] <= num_pages, "free_pages must be [<= num_pages]")
+        self.free_pages[:init.shape[0]].copy_(init)
+        self.count = torch.tensor([init.shape[0]], dtype=torch.int32, device=self.device)
+
+    def _pool(self) -> _abi.PagePool:
+        return _abi.PagePool(self.free_pages.data_ptr(), self.count.data_ptr(), self.capacity)
+
+    @staticmethod
+    def _table(page_table: torch.Tensor):
+        _check(page_table.dim() == 2 and page_table.dtype == torch.int32 and page_table.stride(1) == 1,
+               "page_table must be int32 [rows, width] with unit column stride")
+        return page_table.data_ptr(), page_table.stride(0), page_table.shape[0], page_table.shape[1]
+
+    def _vec(self, t: torch.Tensor, n: int, name: str) -> int:
+        _check(t.dim() == 1 and t.shape[0] == n and t.dtype == torch.int32 and t.device == self.device
+               and (t.stride(0) == 1 or n <= 1), f"{name} must be contiguous int32 [{n}] on the pool's device")
+        return t.data_ptr()
+
+    def reserve(self, page_table: torch.Tensor, prior_len: torch.Tensor, new_len: torch.Tensor, page_size: int,
+                table_index: torch.Tensor | None = None, error_word: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> None:
+        """Give each sequence the pages its prior_len + new_len tokens lack,
+        written into its page-table row (row table_index[i], default i)."""
+        B = prior_len.shape[0]
+        a = _abi.ReserveArgs()
+        a.pool = self._pool()
+        a.page_table, a.page_table_stride, a.num_table_rows, a.max_pages_per_row = self._table(page_table)
+        a.prior_len = self._vec(prior_len, B, "prior_len")
+        a.new_len = self._vec(new_len, B, "new_len")
+        a.table_index = self._vec(table_index, B, "table_index") if table_index is not None else None
+        a.page_size, a.batch_size = page_size, B
+        a.error_word = error_word.data_ptr() if error_word is not None else None
+        _abi.check(_abi.reserve_pages_raw(a, _stream(stream, self.device)))
+
+    def release(self, page_table: torch.Tensor, rows: torch.Tensor, num_tokens: torch.Tensor, page_size: int,
+                error_word: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """Return the pages of each row (ceil(num_tokens / page_size)) to the
+        list, in row order, and clear those table entries to -1."""
+        R = rows.shape[0]
+        a = _abi.ReleaseArgs()
+        a.pool = self._pool()
+        a.page_table, a.page_table_stride, a.num_table_rows, a.max_pages_per_row = self._table(page_table)
+        a.rows = self._vec(rows, R, "rows")
+        a.num_tokens = self._vec(num_tokens, R, "num_tokens")
+        a.page_size, a.num_release = page_size, R
+        a.error_word = error_word.data_ptr() if error_word is not None else None
+        _abi.check(_abi.release_pages_raw(a, _stream(stream, self.device)))
+
+    def free_count(self) -> int:
+        return int(self.count.item())
+
+    def free_list(self) -> torch.Tensor:
+        return self.free_pages[:self.free_count()].clone()
