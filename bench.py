@@ -541,6 +541,8 @@ def run_ours(args, world, rank, local):
         line["embedding_gather"] = bench_gather(dev, peak)
     if not args.no_qkv:
         line["qkv_norm_rope_store"] = bench_qkv(dev, peak)
+    if not args.no_pool:
+        line["page_allocator"] = bench_pool(dev)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_store_step_sample(b0, seconds=args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -641,6 +643,72 @@ def bench_qkv(dev, peak: float) -> dict:
     return out
 
 
+def bench_pool(dev, B: int = 256, ps: int = 16, steps: int = 256) -> dict:
+    """Page allocation per decode step for a Llama-3-8B-sized batch (256
+    sequences, one new token each, page 16): the device pool
+    (yl_reserve_pages, one launch, lengths advanced on the device) against the
+    host KVCacheManager path it replaces (per-request Reserve, then the
+    page-table sync to the device), timed over `steps` consecutive steps."""
+    C = yl.load_extension()
+    W = 80  # 512 prior + 2 * 256 timed + 256 warm-up tokens = 80 pages of 16
+    P = B * W
+    rng = np.random.default_rng(12)
+    prior0 = rng.integers(128, 512, B).astype(np.int32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
+
+    def fresh():
+        pool = yl.DevicePagePool(P, dev)
+        table = torch.full((B, W), -1, dtype=torch.int32, device=dev)
+        pool.reserve(table, t(np.zeros(B)), t(prior0), ps)
+        return pool, table, t(prior0)
+
+    ones = torch.ones(B, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    pool, table, prior = fresh()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(steps):
+            pool.reserve(table, prior, ones, ps, error_word=err)
+            prior.add_(ones)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        for _ in range(steps):
+            prior.add_(ones)
+    # capture ran nothing; one untimed replay each, then the timed one (two
+    # replays add 2 * steps / ps pages per sequence: the pool and rows hold them)
+    g.replay()
+    g2.replay()
+    torch.cuda.synchronize()
+    both = time_graphs([g]) * 1e3 / steps
+    add_only = time_graphs([g2]) * 1e3 / steps
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    del g, g2
+
+    m = C.KVCacheManager(P, B, W, ps, str(dev))
+    rows = [m.AllocateTableSlot() for _ in range(B)]
+    lens = prior0.astype(np.int64).copy()
+    for i in range(B):
+        m.Reserve(rows[i], int(lens[i]))
+    m.SyncPageTable()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lens += 1
+        for i in range(B):
+            m.Reserve(rows[i], int(lens[i]))
+        m.SyncPageTable()
+    torch.cuda.synchronize()
+    host_us = (time.perf_counter() - t0) * 1e6 / steps
+    return {"workload": f"decode, {B} sequences, 1 token each, page {ps}, {steps} consecutive steps",
+            "device_reserve_us": round(both - add_only, 3),
+            "device_timing": "one yl_reserve_pages launch per step in a CUDA graph, minus the same graph's "
+                             "length update alone",
+            "host_manager_us": round(host_us, 2),
+            "host_timing": "wall clock of KVCacheManager.Reserve per request + SyncPageTable per step (C++ front "
+                           "end called from Python)"}
+
+
 def run_e2e(args, steps, k_pool, v_pool, err, world):
     """The same step through the public API with host inputs: every step
     copies its K/V rows, lengths and page table from pinned host memory,
@@ -701,6 +769,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-gather", action="store_true", help="skip the embedding-gather line")
     ap.add_argument("--no-qkv", action="store_true", help="skip the fused norm/rotary/store line")
+    ap.add_argument("--no-pool", action="store_true", help="skip the page-allocator line")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
