@@ -33,10 +33,11 @@
 namespace ylk {
 
 constexpr int kIndexThreads = 256;     // small batches: many blocks, cheap redundant scans
-constexpr int kIndexThreadsBig = 1024; // batches above kBigBatch: 4x fewer blocks repeat the scan
-constexpr int kBigBatch = 1024;
+constexpr int kIndexThreadsBig = 1024; // batches above kBigBatch: 4x fewer blocks repeat the scan, loads batched
+constexpr int kBigBatch = 512;
 constexpr int kScanThreads = 1024;     // one-block scan of the two-launch form
 constexpr int kSmemBatchLimit = 16384;
+constexpr int kFillUnroll = 4;          // fill elements in flight per thread in the big-batch kernels
 
 // Single-launch form (B <= kSmemBatchLimit).
 template <int THREADS>
@@ -47,17 +48,21 @@ __global__ void __launch_bounds__(THREADS) build_index_kernel(const __grid_const
   int32_t *qop = kvp + (p.batch + 1);                        // [B+1]
   const bool report = blockIdx.x == 0;
   pdl_trigger();  // a store launched as our dependent may start loading its K/V rows now
-  if (!scan_batch(p, kvp, qop, scratch, report)) return;
+  constexpr bool kBig = THREADS == kIndexThreadsBig;
+  if (!scan_batch<kBig>(p, kvp, qop, scratch, report)) return;
   write_seq_outputs(p, kvp, qop, static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
                     static_cast<int64_t>(gridDim.x) * blockDim.x, true);
-  fill_block_share(p, kvp, qop, report);
+  if constexpr (kBig)
+    fill_block_share<kFillUnroll>(p, kvp, qop, report, fill_by_sequence_suits(p, kvp, scanned_max_pages(scratch)));
+  else
+    fill_block_share<1>(p, kvp, qop, report);
 }
 
 // Two-launch form, launch 1 (one block): scan straight into the outputs.  On
 // overflow kv_indptr[B] is set to -1 so that launch 2 skips the fill.
 __global__ void __launch_bounds__(kScanThreads) scan_index_kernel(const __grid_constant__ IndexParams p) {
   __shared__ int64_t scratch[kScanScratch];
-  if (!scan_batch(p, p.kv_indptr, p.qo_indptr, scratch, true)) {
+  if (!scan_batch<true>(p, p.kv_indptr, p.qo_indptr, scratch, true)) {
     if (threadIdx.x == 0) p.kv_indptr[p.batch] = -1;
     return;
   }
@@ -68,7 +73,28 @@ __global__ void __launch_bounds__(kScanThreads) scan_index_kernel(const __grid_c
 __global__ void __launch_bounds__(kIndexThreadsBig) fill_index_kernel(const __grid_constant__ IndexParams p) {
   pdl_trigger();
   if (p.kv_indptr[p.batch] < 0) return;
-  fill_block_share(p, p.kv_indptr, p.qo_indptr, blockIdx.x == 0);
+  // the batch's largest page count, from the scanned offsets (each block
+  // reads them once, kStageUnroll per thread in flight)
+  __shared__ int32_t s_max;
+  if (threadIdx.x == 0) s_max = 0;
+  __syncthreads();
+  int32_t mx = 0;
+  for (int base = threadIdx.x; base < p.batch; base += kStageUnroll * blockDim.x) {
+    int32_t d[kStageUnroll];
+#pragma unroll
+    for (int u = 0; u < kStageUnroll; ++u) {
+      const int i = base + u * static_cast<int>(blockDim.x);
+      d[u] = i < p.batch ? __ldg(p.kv_indptr + i + 1) - __ldg(p.kv_indptr + i) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kStageUnroll; ++u) mx = max(mx, d[u]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(&s_max, mx);
+  __syncthreads();
+  fill_block_share<kFillUnroll>(p, p.kv_indptr, p.qo_indptr, blockIdx.x == 0,
+                                fill_by_sequence_suits(p, p.kv_indptr, s_max));
 }
 
 static size_t single_launch_smem(int batch) { return kScanScratch * sizeof(int64_t) + 2 * (batch + 1) * sizeof(int32_t); }

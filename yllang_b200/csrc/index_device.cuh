@@ -39,8 +39,15 @@ struct IndexParams {
   int64_t expected_tokens;  // step only: the store's N, checked against the sum of new_len (-1: no check)
 };
 
-// int64 words of shared scratch the scan needs: 2 x 32 warp totals + 2 block totals.
-constexpr int kScanScratch = 66;
+// int64 words of shared scratch the scan needs: 2 x 32 warp totals, 2 block
+// totals, and one word whose low half holds the batch's largest page count.
+constexpr int kScanScratch = 67;
+constexpr int kScanMaxWord = 66;
+
+// Largest page count of any sequence, after scan_batch<true>.
+__device__ __forceinline__ int32_t scanned_max_pages(const int64_t *scratch) {
+  return reinterpret_cast<const int32_t *>(scratch)[2 * kScanMaxWord];
+}
 
 struct SeqFacts {
   int32_t prior;  // clamped to >= 0
@@ -49,12 +56,11 @@ struct SeqFacts {
   int32_t row;    // page-table row
 };
 
-// Validated per-sequence facts.  Only `report` threads raise error bits so a
-// bad input is not reported once per block.
-__device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool report) {
+// Validated per-sequence facts from the sequence's loaded prior length, new
+// length and table row.  Only `report` threads raise error bits so a bad
+// input is not reported once per block.
+__device__ __forceinline__ SeqFacts facts_of(const IndexParams &p, int32_t pl, int32_t nl, int32_t row, bool report) {
   SeqFacts f;
-  int32_t pl = p.prior_len[i];
-  int32_t nl = p.new_len[i];
   if (pl < 0 || nl < 0) {
     if (report) raise_deverr(p.error_word, YL_DEVERR_NEGATIVE_LEN);
     pl = max(pl, 0);
@@ -62,14 +68,11 @@ __device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool 
   }
   f.prior = pl;
   f.fresh = nl;
-  f.row = i;
+  f.row = row;
   bool row_ok = true;
-  if (p.table_index != nullptr) {
-    f.row = p.table_index[i];
-    if (f.row < 0 || f.row >= p.num_table_rows) {
-      if (report) raise_deverr(p.error_word, YL_DEVERR_TABLE_ROW);
-      row_ok = false;
-    }
+  if (p.table_index != nullptr && (row < 0 || row >= p.num_table_rows)) {
+    if (report) raise_deverr(p.error_word, YL_DEVERR_TABLE_ROW);
+    row_ok = false;
   }
   const int64_t total = static_cast<int64_t>(pl) + nl;
   int64_t np = 0;
@@ -85,20 +88,64 @@ __device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool 
   return f;
 }
 
+__device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool report) {
+  return facts_of(p, p.prior_len[i], p.new_len[i], p.table_index != nullptr ? p.table_index[i] : i, report);
+}
+
+// Sequences staged per thread per round of the scan (their loads in flight together).
+constexpr int kStageUnroll = 8;
+
 // Phase A: scan page and token counts of all sequences into kvp[0..B] and
 // qop[0..B] (shared or global memory).  The counts are first staged in
 // kvp/qop (coalesced); each warp then scans its contiguous segment 32 entries
 // at a time with shuffles (conflict-free), the warp totals are scanned once,
 // and each warp adds its offset.  Returns false (uniformly across the block)
 // when a sum passes INT32_MAX; the fill must then be skipped.
+// kBig (the big-batch kernels): the counts are staged kStageUnroll
+// sequences per thread per round with their loads in flight together, and
+// the batch's largest page count is kept for the fill's choice; otherwise one
+// sequence per thread per pass (small batches: at most a pass or two).
+template <bool kBig = false>
 __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *qop, int64_t *scratch, bool report) {
   const int B = p.batch;
-  for (int i = threadIdx.x; i < B; i += blockDim.x) {
-    const SeqFacts f = seq_facts(p, i, report);
-    kvp[i] = f.pages;
-    qop[i] = f.fresh;
+  if constexpr (!kBig) {
+    for (int i = threadIdx.x; i < B; i += blockDim.x) {
+      const SeqFacts f = seq_facts(p, i, report);
+      kvp[i] = f.pages;
+      qop[i] = f.fresh;
+    }
+    __syncthreads();
+  } else {
+  int32_t max_pages = 0;
+  if (threadIdx.x == 0) reinterpret_cast<int32_t *>(scratch)[2 * kScanMaxWord] = 0;
+  for (int base = threadIdx.x; base < B; base += kStageUnroll * blockDim.x) {
+    int32_t pl[kStageUnroll], nl[kStageUnroll], rw[kStageUnroll];
+#pragma unroll
+    for (int u = 0; u < kStageUnroll; ++u) {
+      const int i = base + u * static_cast<int>(blockDim.x);
+      if (i < B) {
+        pl[u] = __ldg(p.prior_len + i);
+        nl[u] = __ldg(p.new_len + i);
+        rw[u] = p.table_index != nullptr ? __ldg(p.table_index + i) : i;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStageUnroll; ++u) {
+      const int i = base + u * static_cast<int>(blockDim.x);
+      if (i < B) {
+        const SeqFacts f = facts_of(p, pl[u], nl[u], rw[u], report);
+        kvp[i] = f.pages;
+        qop[i] = f.fresh;
+        max_pages = max(max_pages, f.pages);
+      }
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) max_pages = max(max_pages, __shfl_xor_sync(0xffffffffu, max_pages, o));
+  __syncthreads();  // the max word's reset is visible before any update
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int32_t *>(scratch) + 2 * kScanMaxWord, max_pages);
   __syncthreads();
+  }
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
@@ -236,30 +283,49 @@ __device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_
 }
 
 // Phase C for the elements [begin, end) of [kv_indices | slot_mapping]: one
-// element per thread per pass, its sequence found by a branchless search over
+// element per thread per pass (U per pass for big batches), its sequence
+// found by a branchless search over
 // the scanned offsets, gathered from that sequence's page-table row
 // (coalesced row reads and output writes).  The whole fill space is below
 // 2^31 elements (checked on the host), so element arithmetic is 32-bit.
 // Slot entries past qo_indptr[B] (up to the slot capacity) are written as -1.
 // Each element belongs to exactly one block, so every block reports its own.
-// Measured on B200 and slower: warp-cooperative searches (two per chunk,
-// then a per-lane search of the chunk's span), multi-element unrolled passes,
-// and per-block walks over the spanned sequences (the decode batch is
-// latency-bound at one element per thread; any serial per-block search lands
-// on its critical path).
+// Measured on B200 and slower for the decode batch (under one element per
+// thread): warp-cooperative searches (two per chunk, then a per-lane search
+// of the chunk's span), multi-element unrolled passes, and per-block walks
+// over the spanned sequences (latency-bound at one element per thread; any
+// serial per-block search lands on its critical path).
+template <int U>
 __device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, const int32_t *qop, int32_t n_idx,
                                   int32_t begin, int32_t end) {
   const int32_t n_tok = qop[p.batch];
   const int top = pow2_floor(p.batch);
   const int32_t kv_end = min(end, n_idx);
-  for (int32_t e = begin + static_cast<int32_t>(threadIdx.x); e < kv_end; e += blockDim.x) {
-    const int i = find_seq32(kvp, p.batch, e, top);
-    const int32_t row = p.table_index ? __ldg(p.table_index + i) : i;
-    const int32_t page = __ldg(p.page_table + static_cast<int64_t>(row) * p.page_table_stride + (e - kvp[i]));
-    if (p.num_pages > 0 && (page < 0 || page >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
-    p.kv_indices[e] = page;
+  const int32_t step = static_cast<int32_t>(blockDim.x);
+  // U elements per thread per pass: every search, then every page-table load,
+  // then every store, so a thread with several elements has them in flight
+  // together (the big-batch kernel; U = 1 elsewhere).
+  for (int32_t e0 = begin + static_cast<int32_t>(threadIdx.x); e0 < kv_end; e0 += U * step) {
+    int seq[U];
+    int32_t page[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) seq[u] = e0 + u * step < kv_end ? find_seq32(kvp, p.batch, e0 + u * step, top) : -1;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (seq[u] >= 0) {
+        const int32_t row = p.table_index ? __ldg(p.table_index + seq[u]) : seq[u];
+        page[u] = __ldg(p.page_table + static_cast<int64_t>(row) * p.page_table_stride + (e0 + u * step - kvp[seq[u]]));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (seq[u] >= 0) {
+        if (p.num_pages > 0 && (page[u] < 0 || page[u] >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
+        p.kv_indices[e0 + u * step] = page[u];
+      }
+    }
   }
-  for (int32_t e = max(begin, n_idx) + static_cast<int32_t>(threadIdx.x); e < end; e += blockDim.x) {
+  for (int32_t e = max(begin, n_idx) + static_cast<int32_t>(threadIdx.x); e < end; e += step) {
     const int32_t t = e - n_idx;
     int64_t slot = -1;
     if (t < n_tok) {
@@ -268,6 +334,68 @@ __device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, cons
     }
     write_slot(p, t, slot);
   }
+}
+
+// kv_indices by sequence: each sequence's page-table row is copied by wps
+// warps of the grid (wps = warps in the grid / B, 1 to 8; warp part q of a
+// sequence takes its pages q*32 + lane + 32*wps*k), kSeqCopyUnroll pages per
+// lane in flight; no search.  For batches with more pages than threads,
+// where the per-element search's instructions dominate.
+constexpr int kSeqCopyUnroll = 4;
+__device__ inline void fill_kv_by_sequence(const IndexParams &p, const int32_t *kvp, int32_t n_idx) {
+  const int lane = threadIdx.x & 31;
+  const int warps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
+  const int wps = max(1, min(8, warps / max(p.batch, 1)));
+  const int gw = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int part = gw % wps;
+  const int stride = 32 * wps;
+  for (int i = gw / wps; i < p.batch; i += warps / wps) {
+    const int32_t off = kvp[i];
+    const int32_t n = min(kvp[i + 1], n_idx) - off;  // the capacity clamps the tail
+    if (n <= 0) continue;
+    const int32_t row = p.table_index ? __ldg(p.table_index + i) : i;
+    const int32_t *src = p.page_table + static_cast<int64_t>(row) * p.page_table_stride;
+    int32_t *dst = p.kv_indices + off;
+    for (int32_t j0 = part * 32 + lane; j0 < n; j0 += stride * kSeqCopyUnroll) {
+      int32_t page[kSeqCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kSeqCopyUnroll; ++u)
+        if (j0 + stride * u < n) page[u] = __ldg(src + j0 + stride * u);
+#pragma unroll
+      for (int u = 0; u < kSeqCopyUnroll; ++u) {
+        if (j0 + stride * u < n) {
+          if (p.num_pages > 0 && (page[u] < 0 || page[u] >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
+          dst[j0 + stride * u] = page[u];
+        }
+      }
+    }
+  }
+}
+
+// Slots of tokens [0, slot capacity), grid-strided over threads (entries past
+// qo_indptr[B] are -1).
+__device__ inline void fill_slots_strided(const IndexParams &p, const int32_t *kvp, const int32_t *qop) {
+  const int32_t n_tok = qop[p.batch];
+  const int top = pow2_floor(p.batch);
+  const int64_t n_slot = p.slot_mapping ? p.slots_cap : 0;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n_slot;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t slot = -1;
+    if (t < n_tok) {
+      const int i = find_seq32(qop, p.batch, static_cast<int32_t>(t), top);
+      slot = slot_at(p, kvp, i, static_cast<int64_t>(max(__ldg(p.prior_len + i), 0)) + (t - qop[i]));
+    }
+    write_slot(p, t, slot);
+  }
+}
+
+// True when the sequence-warp fill suits the batch: more pages than threads
+// in the grid (else one element per thread is already a single pass), at
+// least 32 pages per sequence on average (a warp's lanes busy) and no
+// sequence above 2,048 pages (no warp left copying long after the others).
+__device__ __forceinline__ bool fill_by_sequence_suits(const IndexParams &p, const int32_t *kvp, int32_t max_pages) {
+  return p.batch > 0 && kvp[p.batch] > static_cast<int64_t>(gridDim.x) * blockDim.x &&
+         kvp[p.batch] >= 32ll * p.batch && max_pages <= 2048;
 }
 
 // Phase B: per-sequence outputs for i in [first, B], stepping by `step`.
@@ -288,8 +416,9 @@ __device__ inline void write_seq_outputs(const IndexParams &p, const int32_t *kv
 
 // Split of the fill space [kv_indices | slot_mapping] among blocks, with the
 // capacity and token-count checks.
+template <int U>
 __device__ __forceinline__ void fill_block_share(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
-                                                 bool report) {
+                                                 bool report, bool by_sequence = false) {
   if (report && threadIdx.x == 0 && p.expected_tokens >= 0 && qop[p.batch] != p.expected_tokens)
     raise_deverr(p.error_word, YL_DEVERR_TOKEN_COUNT);
   int64_t n_idx = p.kv_indices ? kvp[p.batch] : 0;
@@ -300,12 +429,17 @@ __device__ __forceinline__ void fill_block_share(const IndexParams &p, const int
   }
   if (p.slot_mapping && qop[p.batch] > p.slots_cap && report && threadIdx.x == 0)
     raise_deverr(p.error_word, YL_DEVERR_SLOTS_CAP);
+  if (by_sequence) {
+    fill_kv_by_sequence(p, kvp, static_cast<int32_t>(n_idx));
+    fill_slots_strided(p, kvp, qop);
+    return;
+  }
   const int64_t work = n_idx + n_slot;  // < 2^31 (checked on the host)
   const int64_t chunk = (work + gridDim.x - 1) / gridDim.x;
   const int64_t begin = static_cast<int64_t>(blockIdx.x) * chunk;
   const int64_t end = min(begin + chunk, work);
   if (begin < end)
-    fill_range(p, kvp, qop, static_cast<int32_t>(n_idx), static_cast<int32_t>(begin), static_cast<int32_t>(end));
+    fill_range<U>(p, kvp, qop, static_cast<int32_t>(n_idx), static_cast<int32_t>(begin), static_cast<int32_t>(end));
 }
 
 // kv_indices share of this block when the slots of tokens [0, slot_begin) are

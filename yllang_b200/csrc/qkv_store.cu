@@ -21,8 +21,9 @@
 // * qkv_tma_kernel: one CTA per SM; a producer warp streams tiles of whole
 //   tokens (Q, K, V rows and the token's cos/sin row) into a ring of shared
 //   memory stages with bulk copies completing on mbarriers, 16 consumer warps
-//   take the chunks of a landed stage.  The bytes in flight live in shared
-//   memory (about 190 KB per SM) instead of registers, which is what HBM
+//   take the chunks of a landed stage (6 stages of 2-3 tokens by default).
+//   The bytes in flight live in shared memory (up to 227 KB per SM)
+//   instead of registers, which is what HBM
 //   latency x bandwidth asks for at prefill sizes.  Every mbarrier wait is
 //   bounded; a timeout sets YL_DEVERR_TIMEOUT and the CTA drains its copies
 //   and exits.
@@ -82,6 +83,7 @@ struct QkvParams {
   uint32_t num_tiles;
   uint32_t token_bytes;  // Q + K + V rows (+ cos/sin row) of one token in a stage
   uint32_t stage_bytes;  // meta + tile_tokens * token_bytes
+  uint32_t num_stages;   // <= kQkvMaxStages
 };
 
 // 16-bit element types: a pair of elements is one 32-bit word, low half first.
@@ -399,19 +401,19 @@ __global__ void __launch_bounds__(256) qkv_norm_rope_store_kernel(const __grid_c
 // ---------------------------------------------------------------------------
 // TMA-staged kernel
 // ---------------------------------------------------------------------------
-constexpr int kQkvStages = 3;
-constexpr int kQkvConsumerWarps = 16;
-constexpr int kQkvThreads = 32 * (1 + kQkvConsumerWarps);
+constexpr uint32_t kQkvMaxStages = 16;
 constexpr uint32_t kQkvMetaBytes = 32 * 16;  // per stage: int64 position and slot of up to 32 tokens
-constexpr uint32_t kQkvBarrierBytes = 128;
+constexpr uint32_t kQkvBarrierBytes = 2 * kQkvMaxStages * 8;
 constexpr uint64_t kQkvWaitNs = 2000000000ull;  // 2 s
 
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(kQkvThreads, 1) qkv_tma_kernel(const __grid_constant__ QkvParams p) {
+// CW consumer warps, chunks of G heads.
+template <typename T, int D, int G, int CW>
+__global__ void __launch_bounds__(32 * (1 + CW), 1) qkv_tma_kernel(const __grid_constant__ QkvParams p) {
   constexpr uint32_t ROW_BYTES = D * 2;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-  uint64_t *empty = full + kQkvStages;
+  uint64_t *empty = full + kQkvMaxStages;
+  const uint32_t S = p.num_stages;
   unsigned char *stages = smem + kQkvBarrierBytes;
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
@@ -420,9 +422,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_tma_kernel(const __grid_co
   const bool rope = p.cos_sin != nullptr;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kQkvStages; ++s) {
+    for (uint32_t s = 0; s < S; ++s) {
       mbar_init(&full[s], 32);                  // every producer lane arrives
-      mbar_init(&empty[s], kQkvConsumerWarps);  // one arrival per consumer warp
+      mbar_init(&empty[s], CW);  // one arrival per consumer warp
     }
     fence_mbar_init();
   }
@@ -447,8 +449,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_tma_kernel(const __grid_co
     for (uint32_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++iter) {
       const int64_t slot = next_slot, pos = next_pos;
       fetch(tile + gridDim.x);
-      const uint32_t s = iter % kQkvStages;
-      if (iter >= kQkvStages && !mbar_wait_bounded(&empty[s], ((iter / kQkvStages) - 1) & 1u, kQkvWaitNs)) {
+      const uint32_t s = iter % S;
+      if (iter >= S && !mbar_wait_bounded(&empty[s], ((iter / S) - 1) & 1u, kQkvWaitNs)) {
         if (lane == 0) raise_deverr(p.error_word, YL_DEVERR_TIMEOUT);
         break;
       }
@@ -475,9 +477,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_tma_kernel(const __grid_co
       if (lane != 0) mbar_arrive(&full[s]);
     }
     // no copy may land after the CTA exits: wait for the phases armed last
-    const uint32_t first = iter > kQkvStages ? iter - kQkvStages : 0;
+    const uint32_t first = iter > S ? iter - S : 0;
     for (uint32_t j = first; j < iter; ++j) {
-      if (!mbar_wait_bounded(&full[j % kQkvStages], (j / kQkvStages) & 1u, kQkvWaitNs)) {
+      if (!mbar_wait_bounded(&full[j % S], (j / S) & 1u, kQkvWaitNs)) {
         if (lane == 0) raise_deverr(p.error_word, YL_DEVERR_TIMEOUT);
         break;
       }
@@ -492,8 +494,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_tma_kernel(const __grid_co
   const uint32_t lane_off = (lane & 15u) * L::SEG + (lane >> 4) * L::ROW;
   uint32_t iter = 0;
   for (uint32_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++iter) {
-    const uint32_t s = iter % kQkvStages;
-    if (!mbar_wait_bounded(&full[s], (iter / kQkvStages) & 1u, kQkvWaitNs)) {
+    const uint32_t s = iter % S;
+    if (!mbar_wait_bounded(&full[s], (iter / S) & 1u, kQkvWaitNs)) {
       if (lane == 0) raise_deverr(p.error_word, YL_DEVERR_TIMEOUT);
       break;
     }
@@ -501,7 +503,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_tma_kernel(const __grid_co
     const int64_t *meta = reinterpret_cast<const int64_t *>(stage);
     const uint32_t t0 = tile * p.tile_tokens;
     const uint32_t nt = min(p.tile_tokens, p.num_tokens - t0);
-    for (uint32_t u = cw; u < nt * p.chunks; u += kQkvConsumerWarps) {
+    for (uint32_t u = cw; u < nt * p.chunks; u += CW) {
       const uint32_t t = p.by_chunks.div(u);
       int kind;
       uint32_t h0, nh;
@@ -549,9 +551,17 @@ namespace {
 using ylk::QkvParams;
 using Kernel = void (*)(QkvParams);
 
+// A TMA kernel shape: chunks of g heads, cw consumer warps.
+struct TmaShape {
+  Kernel fn;
+  uint32_t g;
+  uint32_t cw;
+};
+
 struct QkvKernels {
-  Kernel small, big, tma;
+  Kernel small, big;
   uint32_t g_big;
+  TmaShape tma[4];  // [0] is the default; YL_QKV_TMA_SHAPE picks another
 };
 
 template <typename T>
@@ -559,14 +569,52 @@ QkvKernels qkv_kernels(int head_dim) {
   using namespace ylk;
   switch (head_dim) {
     case 64:
-      return {qkv_norm_rope_store_kernel<T, 64, 2>, qkv_norm_rope_store_kernel<T, 64, 8>, qkv_tma_kernel<T, 64, 8>, 8};
+      return {qkv_norm_rope_store_kernel<T, 64, 2>,
+              qkv_norm_rope_store_kernel<T, 64, 8>,
+              8,
+              {{qkv_tma_kernel<T, 64, 8, 16>, 8, 16},
+               {qkv_tma_kernel<T, 64, 4, 24>, 4, 24},
+               {qkv_tma_kernel<T, 64, 4, 31>, 4, 31},
+               {qkv_tma_kernel<T, 64, 2, 31>, 2, 31}}};
     case 128:
-      return {qkv_norm_rope_store_kernel<T, 128, 2>, qkv_norm_rope_store_kernel<T, 128, 8>, qkv_tma_kernel<T, 128, 8>,
-              8};
+      return {qkv_norm_rope_store_kernel<T, 128, 2>,
+              qkv_norm_rope_store_kernel<T, 128, 8>,
+              8,
+              {{qkv_tma_kernel<T, 128, 8, 16>, 8, 16},
+               {qkv_tma_kernel<T, 128, 4, 24>, 4, 24},
+               {qkv_tma_kernel<T, 128, 4, 31>, 4, 31},
+               {qkv_tma_kernel<T, 128, 2, 31>, 2, 31}}};
     default:
-      return {qkv_norm_rope_store_kernel<T, 256, 2>, qkv_norm_rope_store_kernel<T, 256, 4>, qkv_tma_kernel<T, 256, 4>,
-              4};
+      return {qkv_norm_rope_store_kernel<T, 256, 2>,
+              qkv_norm_rope_store_kernel<T, 256, 4>,
+              4,
+              {{qkv_tma_kernel<T, 256, 4, 16>, 4, 16},
+               {qkv_tma_kernel<T, 256, 2, 24>, 2, 24},
+               {qkv_tma_kernel<T, 256, 2, 31>, 2, 31},
+               {qkv_tma_kernel<T, 256, 2, 31>, 2, 31}}};
   }
+}
+
+// YL_QKV_STAGES=2..16 sets the TMA kernel's number of stages (default 6:
+// 3 to 8 measured within 3 % of each other at prefill sizes, 12 and more
+// slower).
+uint32_t qkv_stages() {
+  static const uint32_t v = [] {
+    const char *e = std::getenv("YL_QKV_STAGES");
+    const int i = e ? std::atoi(e) : 6;
+    return static_cast<uint32_t>(i >= 2 && i <= static_cast<int>(ylk::kQkvMaxStages) ? i : 6);
+  }();
+  return v;
+}
+
+// YL_QKV_TMA_SHAPE=0..3 picks a TMA kernel shape (for tuning runs).
+int qkv_tma_shape() {
+  static const int v = [] {
+    const char *e = std::getenv("YL_QKV_TMA_SHAPE");
+    const int i = e ? std::atoi(e) : 0;
+    return i >= 0 && i < 4 ? i : 0;
+  }();
+  return v;
 }
 
 void set_chunks(QkvParams &p, uint32_t G) {
@@ -678,8 +726,15 @@ extern "C" int yl_qkv_norm_rope_store(const yl_qkv_store_args *a, cudaStream_t s
   // and its bulk copies are legal: 16-byte aligned sources and strides, and
   // one token's rows fit a stage.
   const uint64_t token_bytes = static_cast<uint64_t>(q_row + 2 * kv_row) + (a->cos_sin_cache ? D * 4 : 0);
-  const uint64_t stage_budget = (227u * 1024u - kQkvBarrierBytes) / kQkvStages;
-  uint64_t tile_tokens = stage_budget > kQkvMetaBytes + 128 ? (stage_budget - kQkvMetaBytes - 127) / token_bytes : 0;
+  // S stages of equal size share 227 KB of shared memory; a stage holds
+  // tile_tokens whole tokens (at most 32, at least 1, else no TMA kernel)
+  uint32_t S = qkv_stages();
+  uint64_t tile_tokens = 0;
+  for (; S >= 2; --S) {
+    const uint64_t stage_budget = (227u * 1024u - kQkvBarrierBytes) / S;
+    tile_tokens = stage_budget > kQkvMetaBytes + 127 ? (stage_budget - kQkvMetaBytes - 127) / token_bytes : 0;
+    if (tile_tokens >= 1) break;
+  }
   if (tile_tokens > 32) tile_tokens = 32;
   const uintptr_t bulk_bits = reinterpret_cast<uintptr_t>(a->k) | reinterpret_cast<uintptr_t>(a->v) |
                               static_cast<uintptr_t>(a->k_row_stride) | static_cast<uintptr_t>(a->v_row_stride) |
@@ -696,17 +751,19 @@ extern "C" int yl_qkv_norm_rope_store(const yl_qkv_store_args *a, cudaStream_t s
   if (qkv_engine_override() == 2 && tma_legal) engine = 2;
 
   if (engine == 2) {
-    set_chunks(p, ks.g_big);
+    const TmaShape &shape = ks.tma[qkv_tma_shape()];
+    set_chunks(p, shape.g);
     p.tile_tokens = static_cast<uint32_t>(tile_tokens);
     p.num_tiles = static_cast<uint32_t>(tiles);
     p.token_bytes = static_cast<uint32_t>(token_bytes);
     p.stage_bytes = static_cast<uint32_t>((kQkvMetaBytes + tile_tokens * token_bytes + 127) / 128 * 128);
-    const size_t smem = kQkvBarrierBytes + static_cast<size_t>(kQkvStages) * p.stage_bytes;
-    if (cudaFuncSetAttribute(ks.tma, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+    p.num_stages = S;
+    const size_t smem = kQkvBarrierBytes + static_cast<size_t>(S) * p.stage_bytes;
+    if (cudaFuncSetAttribute(shape.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return check_launch("yl_qkv_norm_rope_store: shared memory attribute");
     const uint64_t grid = tiles < sms ? tiles : sms;
-    ks.tma<<<static_cast<unsigned>(grid), kQkvThreads, smem, stream>>>(p);
+    shape.fn<<<static_cast<unsigned>(grid), 32 * (1 + shape.cw), smem, stream>>>(p);
     return check_launch("yl_qkv_norm_rope_store launch");
   }
   const Kernel fn = engine == 1 ? ks.big : ks.small;
