@@ -113,6 +113,28 @@ def test_index_large_batch_two_launch_form(cuda):
     assert_index_equal(got, want)
 
 
+@pytest.mark.parametrize("B,tix", [(2048, False), (3000, True), (20000, False)])
+def test_index_big_batch_errors_and_capacity(cuda, B, tix):
+    """Decode-shaped big batches (the warp-per-sequence page copy; 20,000 in
+    the two-launch form) with page ids outside the pool and a kv_indices
+    capacity below the batch's pages: same outputs and error bits as the
+    oracle."""
+    rng = np.random.default_rng(B)
+    prior = rng.integers(100, 4000, B).astype(np.int32)
+    new = np.ones(B, np.int32)
+    ps, P = 16, 1 << 20
+    W = int(-(-(prior.astype(np.int64) + new).max() // ps)) + 1
+    R = B + 11 if tix else B
+    table = rng.integers(0, P, (R, W)).astype(np.int32)
+    rows = rng.permutation(R)[:B].astype(np.int32) if tix else None
+    first = rows[:5] if tix else np.arange(5)
+    table[first, rng.integers(0, 4, 5)] = P + 7  # outside the pool, in pages the first sequences hold
+    total = int(((prior.astype(np.int64) + new + ps - 1) // ps).sum())
+    got, want, err = _run(cuda, prior, new, table, ps, table_index=rows, num_pages=P, kv_cap=total - 1000)
+    assert want["err"] & orc.INDICES_CAP and err == want["err"]
+    assert_index_equal(got, want)
+
+
 def test_index_empty_and_zero_length(cuda):
     got, want, err = _run(cuda, np.zeros(0, np.int32), np.zeros(0, np.int32), np.zeros((1, 4), np.int32), 16)
     assert err == 0 and got["kv_indptr"].tolist() == [0] and got["qo_indptr"].tolist() == [0]
