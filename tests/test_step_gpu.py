@@ -164,3 +164,52 @@ def test_step_other_modes(cuda, mode):
                         os.path.join(here, "test_step_gpu.py"), "-k", "not other_modes"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("tix,slot_dtype", [(False, torch.int64), (True, torch.int64), (False, torch.int32)])
+def test_step_decode_batch_slot_rules(cuda, tix, slot_dtype):
+    """Decode batches (one new token per sequence), where the store computes
+    its own slots beside the index build: page ids outside the pool, a row
+    outside the table, a sequence past its row's pages, a negative prior
+    length and an int32 slot overflow must give the slots, pool and error
+    bits the oracle gives."""
+    rng = np.random.default_rng(7 + int(tix))
+    B, W, ps, E = 300, 16, 16, 256
+    P = (1 << 27) + 5 if slot_dtype == torch.int32 else 6000
+    prior = rng.integers(0, W * ps - 1, B).astype(np.int32)
+    new = np.ones(B, np.int32)
+    R = B + 5 if tix else B
+    # distinct page ids (two tokens on one slot in one call have no defined winner)
+    table = rng.permutation(6000)[:R * W].reshape(R, W).astype(np.int32)
+    rows = rng.permutation(R)[:B].astype(np.int32) if tix else None
+    r_of = (lambda i: rows[i]) if tix else (lambda i: i)
+    prior[3] = W * ps + 20             # past its row's pages: no slot, no store
+    prior[4] = -9                      # clamped to position 0
+    table[r_of(5), prior[5] // ps] = P + 3       # page outside the pool
+    table[r_of(6), prior[6] // ps] = -2          # negative page id
+    if slot_dtype == torch.int32:
+        table[r_of(7), prior[7] // ps] = (1 << 27)  # page * 16 + offset > INT_MAX: no int32 slot
+    if tix:
+        rows[8] = R + 100              # row outside the table
+    S = 6000 * ps + 16
+    g = torch.Generator(device=cuda).manual_seed(1)
+    k = torch.randn(2, B, E, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(2, B, E, generator=g, device=cuda).to(torch.bfloat16)
+    kc = torch.randn(2, S, E, generator=g, device=cuda).to(torch.bfloat16)
+    vc = torch.randn(2, S, E, generator=g, device=cuda).to(torch.bfloat16)
+    want = orc.build_index(prior, new, table, ps, table_index=rows, num_pages=P,
+                           slot_dtype=np.int64 if slot_dtype == torch.int64 else np.int32)
+    want_k, want_v = host_bytes(kc).copy(), host_bytes(vc).copy()
+    orc.store(host_bytes(k), host_bytes(v), want_k, want_v, want["slot_mapping"], num_slots=S)
+    i32 = dict(dtype=torch.int32, device=cuda)
+    out = yl.BatchIndex(torch.empty(B + 1, **i32), torch.empty(int(want["kv_indices"].size), **i32),
+                        torch.empty(B, **i32), torch.empty(B + 1, **i32), torch.empty(B, dtype=slot_dtype, device=cuda))
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    yl.kv_step(_dev(prior, cuda), _dev(new, cuda), _dev(table, cuda), ps, k, v, kc, vc, out,
+               table_index=None if rows is None else _dev(rows, cuda), num_pages=P, error_word=err)
+    torch.cuda.synchronize()
+    assert want["err"] & orc.PAGE_RANGE and int(err.item()) == want["err"]
+    got = index_outputs(out)
+    assert_index_equal(got, want)
+    assert torch.equal(kc.view(torch.uint8).view(-1), torch.from_numpy(want_k.reshape(-1)).to(cuda))
+    assert torch.equal(vc.view(torch.uint8).view(-1), torch.from_numpy(want_v.reshape(-1)).to(cuda))

@@ -40,7 +40,9 @@ constexpr int kSmemBatchLimit = 16384;
 constexpr int kFillUnroll = 4;          // fill elements in flight per thread in the big-batch kernels
 
 // Single-launch form (B <= kSmemBatchLimit).
-template <int THREADS>
+// kBig: batched staging and the choice of the warp-per-sequence fill (the
+// 1024-thread kernel; the 256-thread one too when it runs beside the store).
+template <int THREADS, bool kBig = (THREADS == 1024)>
 __global__ void __launch_bounds__(THREADS) build_index_kernel(const __grid_constant__ IndexParams p) {
   extern __shared__ int64_t smem[];
   int64_t *scratch = smem;                                   // kScanScratch x int64
@@ -48,7 +50,6 @@ __global__ void __launch_bounds__(THREADS) build_index_kernel(const __grid_const
   int32_t *qop = kvp + (p.batch + 1);                        // [B+1]
   const bool report = blockIdx.x == 0;
   pdl_trigger();  // a store launched as our dependent may start loading its K/V rows now
-  constexpr bool kBig = THREADS == kIndexThreadsBig;
   if (!scan_batch<kBig>(p, kvp, qop, scratch, report)) return;
   write_seq_outputs(p, kvp, qop, static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
                     static_cast<int64_t>(gridDim.x) * blockDim.x, true);
@@ -116,6 +117,9 @@ static int ensure_smem_attr() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(build_index_kernel<kIndexThreadsBig>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(single_launch_smem(kSmemBatchLimit)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(build_index_kernel<kIndexThreads, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(single_launch_smem(kSmemBatchLimit)));
     if (e != cudaSuccess) {
       set_last_error(std::string("yl_build_index: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
       return YL_ERR_CUDA;
@@ -178,6 +182,7 @@ int prepare_index(const yl_index_args *a, IndexParams &p) {
   p.slot64 = a->slot_is_int64;
   p.by_page = FastDiv(static_cast<uint32_t>(a->page_size));
   p.expected_tokens = -1;
+  p.beside_store = 0;
 
   return YL_OK;
 }
@@ -187,9 +192,13 @@ int launch_index(const IndexParams &p, cudaStream_t stream) {
   // so big batches use 1024-thread blocks (4x fewer scans), at most one per SM.
   const int64_t work = p.indices_cap + p.slots_cap;
   const int64_t sms = sm_count();
-  const bool big = p.batch > kBigBatch;
+  // beside a store (a decode step whose store computes its own slots): the
+  // 256-thread kernel at two blocks per SM at most, so two of the store's
+  // CTAs fit beside them, with the big-batch staging and fill above 512
+  const bool big = p.batch > kBigBatch && !p.beside_store;
+  const bool big_narrow = p.batch > kBigBatch && p.beside_store;
   const int threads = big ? kIndexThreadsBig : kIndexThreads;
-  const int64_t cap = big ? sms : 4 * sms;
+  const int64_t cap = big ? sms : (p.beside_store ? 2 : 4) * sms;
   int64_t blocks = (work + threads - 1) / threads;
   if (blocks < 1) blocks = 1;
   if (blocks > cap) blocks = cap;
@@ -199,6 +208,8 @@ int launch_index(const IndexParams &p, cudaStream_t stream) {
     if (rc != YL_OK) return rc;
     if (big)
       build_index_kernel<kIndexThreadsBig><<<static_cast<unsigned>(blocks), kIndexThreadsBig, single_launch_smem(p.batch), stream>>>(p);
+    else if (big_narrow)
+      build_index_kernel<kIndexThreads, true><<<static_cast<unsigned>(blocks), kIndexThreads, single_launch_smem(p.batch), stream>>>(p);
     else
       build_index_kernel<kIndexThreads><<<static_cast<unsigned>(blocks), kIndexThreads, single_launch_smem(p.batch), stream>>>(p);
     return check_launch("yl_build_index launch");

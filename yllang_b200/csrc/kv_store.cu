@@ -59,6 +59,40 @@ __global__ void __launch_bounds__(256) store_rows_kernel(const __grid_constant__
   }
 }
 
+// A decode step's store (see yl_kv_step): when every sequence adds one token
+// the kernel computes its slots itself — per row, or with kCached once per
+// CTA into shared memory — and does not wait for the index build; otherwise
+// it waits and reads the slots as store_rows_kernel does.  Separate kernels,
+// so the plain store keeps its own code and registers.
+template <int W, int G, int VPL, int R, typename SlotT, bool kCached>
+__global__ void __launch_bounds__(256) store_rows_self_kernel(const __grid_constant__ StoreParams p) {
+  extern __shared__ int64_t slot_cache[];
+  const uint32_t lane = threadIdx.x % G;
+  const uint32_t group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
+  const uint32_t num_groups = (gridDim.x * blockDim.x) / G;
+
+  uint32_t base = group * R;
+  RowBatch<W, G, VPL, R> b;
+  b.load(p, base, lane);
+  const bool self = decode_batch(p.self);
+  if (!self) pdl_wait();
+  else if (kCached) fill_slot_cache(p.self, slot_cache, p.error_word);  // uniform per block
+  while (base < p.total_rows) {
+    int64_t slot[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      slot[r] = !b.live[r] ? -1
+                : !self    ? load_slot<SlotT>(p.slots, b.token[r])
+                : kCached  ? slot_cache[b.token[r]]
+                           : decode_slot(p.self, b.token[r], p.error_word);
+#pragma unroll
+    for (int r = 0; r < R; ++r) b.resolve(p, r, slot[r]);
+    b.store(lane);
+    base += num_groups * R;
+    if (base < p.total_rows) b.load(p, base, lane);
+  }
+}
+
 // TMA path: one CTA per SM stages its rows in shared memory.  The CTA owns a
 // contiguous range of rows; a round loads up to nslot of them with bulk
 // copies (thread t owns stage slots t, t + 256, ...), so at kernel start
@@ -198,12 +232,23 @@ int fast_vector_bytes() {
   return w;
 }
 
-static bool pick_fast(int64_t row_bytes, int w, bool slot64, StoreVariant &out) {
+// self: 0 the plain store, 1 the decode step's store computing slots per
+// row, 2 the same with the per-CTA slot cache.
+static bool pick_fast(int64_t row_bytes, int w, bool slot64, int self, StoreVariant &out) {
   return dispatch_row_shape(row_bytes, w, [&](auto shape) {
     using S = decltype(shape);
-    out = StoreVariant{slot64 ? store_rows_kernel<S::W, S::G, S::VPL, S::R, int64_t>
-                              : store_rows_kernel<S::W, S::G, S::VPL, S::R, int32_t>,
-                       S::G, S::R};
+    if (self == 1)
+      out = StoreVariant{slot64 ? store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int64_t, false>
+                                : store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int32_t, false>,
+                         S::G, S::R};
+    else if (self == 2)
+      out = StoreVariant{slot64 ? store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int64_t, true>
+                                : store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int32_t, true>,
+                         S::G, S::R};
+    else
+      out = StoreVariant{slot64 ? store_rows_kernel<S::W, S::G, S::VPL, S::R, int64_t>
+                                : store_rows_kernel<S::W, S::G, S::VPL, S::R, int32_t>,
+                         S::G, S::R};
   });
 }
 
@@ -290,6 +335,7 @@ int prepare_store(const yl_store_args *a, bool need_slots, StorePlan &plan) {
   p.cache_layer_stride = multi ? a->cache_layer_stride : 0;
   p.num_slots = a->num_slots;
   p.error_word = a->error_word;
+  p.self = SelfSlots{};
   p.total_rows = static_cast<uint32_t>(total_rows);
   p.row_units = static_cast<uint32_t>(a->row_bytes / plan.unit);
   p.by_tokens = FastDiv(static_cast<uint32_t>(a->num_tokens));
@@ -368,18 +414,21 @@ int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStre
   StoreVariant var{};
   bool fast = false;
   const int w = fast_vector_bytes();
-  if (plan.unit == 16 && w == 32 && (plan.bits & 31u) == 0) fast = pick_fast(row_bytes, 32, slot64, var);
-  if (!fast && plan.unit == 16) fast = pick_fast(row_bytes, 16, slot64, var);
+  const int self = plan.p.self.batch > 0 ? (plan.p.self.cached ? 2 : 1) : 0;
+  if (plan.unit == 16 && w == 32 && (plan.bits & 31u) == 0) fast = pick_fast(row_bytes, 32, slot64, self, var);
+  if (!fast && plan.unit == 16) fast = pick_fast(row_bytes, 16, slot64, self, var);
   if (!fast) var = pick_generic(plan.unit, slot64);
   const uint64_t rows_per_block = static_cast<uint64_t>(kStoreThreads / var.group) * var.rows;
   const uint64_t want = (plan.p.total_rows + rows_per_block - 1) / rows_per_block;
+  // the slot cache of a decode step's store
+  const size_t smem = fast && plan.p.self.cached ? static_cast<size_t>(plan.p.self.batch) * sizeof(int64_t) : 0;
   const uint64_t cap =
-      static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.fn), 0);
+      static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.fn), smem);
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kStoreThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

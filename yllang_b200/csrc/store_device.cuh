@@ -8,11 +8,30 @@
 // reads are in flight while slots are read (or computed) and checked.
 #pragma once
 
+#include <climits>
 #include <cstdint>
 
 #include "common.cuh"
 
 namespace ylk {
+
+// Step only, decode batches: what the store needs to compute a token's slot
+// itself (batch = 0: read the slots the index build writes).
+struct SelfSlots {
+  const int32_t *prior_len;
+  const int32_t *new_len;
+  const int32_t *page_table;
+  const int32_t *table_index;
+  int64_t page_table_stride;
+  int64_t num_pages;
+  int32_t batch;
+  int32_t page_size;
+  int32_t max_pages_per_row;
+  int32_t num_table_rows;
+  int32_t slot64;
+  int32_t cached;  // slots of all `batch` tokens computed once per CTA into shared memory (batch x 8 bytes)
+  FastDiv by_page;
+};
 
 struct StoreParams {
   const char *k;
@@ -31,6 +50,7 @@ struct StoreParams {
   uint32_t total_rows;  // 2 * L * N  (< 2^31)
   uint32_t row_units;   // row_bytes / unit, generic kernel only
   FastDiv by_tokens;    // divides a row id by N
+  SelfSlots self;
 };
 
 // ---------------------------------------------------------------------------
@@ -68,6 +88,56 @@ __device__ __forceinline__ void store_vec(char *p, const Vec<32> &x) {
   asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(x.r[0]), "r"(x.r[1]),
                "r"(x.r[2]), "r"(x.r[3]), "r"(x.r[4]), "r"(x.r[5]), "r"(x.r[6]), "r"(x.r[7])
                : "memory");
+}
+
+// True (on every thread of the block) when every sequence of the batch adds
+// exactly one token, so token t is sequence t's new token and the store can
+// compute slots itself.  Each thread reads its share of new_len.
+__device__ __forceinline__ bool decode_batch(const SelfSlots &s) {
+  int ok = s.batch > 0;
+  for (int i = threadIdx.x; i < s.batch && ok; i += blockDim.x) ok = __ldg(s.new_len + i) == 1;
+  return __syncthreads_and(ok) != 0;
+}
+
+// Slot of token t of a decode batch, by the index build's rules (slot_at
+// over the facts of seq_facts): the prior length clamped at 0; a table row
+// outside the table, or a page past the sequence's pages (its row capped at
+// max_pages_per_row), gives -1 with no bit (the index build reports those);
+// a page id outside the pool, or an int32 slot above INT_MAX, gives -1 and
+// sets YL_DEVERR_PAGE_RANGE.
+__device__ __forceinline__ int64_t decode_slot(const SelfSlots &s, uint32_t t, uint32_t *error_word) {
+  const int32_t pos = max(__ldg(s.prior_len + t), 0);
+  const int32_t row = s.table_index ? __ldg(s.table_index + t) : static_cast<int32_t>(t);
+  if (s.table_index && (row < 0 || row >= s.num_table_rows)) return -1;
+  const int64_t pages = min((static_cast<int64_t>(pos) + s.page_size) / s.page_size,
+                            static_cast<int64_t>(s.max_pages_per_row));  // ceil((pos + 1) / ps), capped
+  const uint32_t pidx = s.by_page.div(static_cast<uint32_t>(pos));
+  if (static_cast<int64_t>(pidx) >= pages) return -1;
+  const int32_t page = __ldg(s.page_table + static_cast<int64_t>(row) * s.page_table_stride + pidx);
+  const bool in_range = page >= 0 && (s.num_pages <= 0 || page < s.num_pages);
+  const int64_t slot = static_cast<int64_t>(page) * s.page_size + (pos - static_cast<int64_t>(pidx) * s.page_size);
+  if (in_range && (s.slot64 || slot <= INT_MAX)) return slot;
+  raise_deverr(error_word, YL_DEVERR_PAGE_RANGE);
+  return -1;
+}
+
+// Every token's slot of a decode batch into shared memory, four tokens per
+// thread per round with their loads in flight together.
+__device__ inline void fill_slot_cache(const SelfSlots &s, int64_t *cache, uint32_t *error_word) {
+  for (int t0 = threadIdx.x; t0 < s.batch; t0 += 4 * blockDim.x) {
+    int64_t v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u * static_cast<int>(blockDim.x);
+      v[u] = t < s.batch ? decode_slot(s, static_cast<uint32_t>(t), error_word) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u * static_cast<int>(blockDim.x);
+      if (t < s.batch) cache[t] = v[u];
+    }
+  }
+  __syncthreads();
 }
 
 template <typename SlotT>
