@@ -166,21 +166,24 @@ def test_step_other_modes(cuda, mode):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 
+@pytest.mark.parametrize("B", [200, 300, 1500])
 @pytest.mark.parametrize("tix,slot_dtype", [(False, torch.int64), (True, torch.int64), (False, torch.int32)])
-def test_step_decode_batch_slot_rules(cuda, tix, slot_dtype):
+def test_step_decode_batch_slot_rules(cuda, B, tix, slot_dtype):
     """Decode batches (one new token per sequence), where the store computes
-    its own slots beside the index build: page ids outside the pool, a row
+    its own slots beside the index build (per row at 200 sequences, cached
+    per CTA at 300, token-major at 1,500): page ids outside the pool, a row
     outside the table, a sequence past its row's pages, a negative prior
     length and an int32 slot overflow must give the slots, pool and error
     bits the oracle gives."""
-    rng = np.random.default_rng(7 + int(tix))
-    B, W, ps, E = 300, 16, 16, 256
-    P = (1 << 27) + 5 if slot_dtype == torch.int32 else 6000
+    rng = np.random.default_rng(7 + int(tix) + B)
+    W, ps, E = 16, 16, 256
+    R = B + 5 if tix else B
+    pool_pages = max(6000, R * W + 16)
+    P = (1 << 27) + 5 if slot_dtype == torch.int32 else pool_pages
     prior = rng.integers(0, W * ps - 1, B).astype(np.int32)
     new = np.ones(B, np.int32)
-    R = B + 5 if tix else B
     # distinct page ids (two tokens on one slot in one call have no defined winner)
-    table = rng.permutation(6000)[:R * W].reshape(R, W).astype(np.int32)
+    table = rng.permutation(pool_pages)[:R * W].reshape(R, W).astype(np.int32)
     rows = rng.permutation(R)[:B].astype(np.int32) if tix else None
     r_of = (lambda i: rows[i]) if tix else (lambda i: i)
     prior[3] = W * ps + 20             # past its row's pages: no slot, no store
@@ -191,7 +194,7 @@ def test_step_decode_batch_slot_rules(cuda, tix, slot_dtype):
         table[r_of(7), prior[7] // ps] = (1 << 27)  # page * 16 + offset > INT_MAX: no int32 slot
     if tix:
         rows[8] = R + 100              # row outside the table
-    S = 6000 * ps + 16
+    S = pool_pages * ps + 16
     g = torch.Generator(device=cuda).manual_seed(1)
     k = torch.randn(2, B, E, generator=g, device=cuda).to(torch.bfloat16)
     v = torch.randn(2, B, E, generator=g, device=cuda).to(torch.bfloat16)

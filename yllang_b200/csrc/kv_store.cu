@@ -93,6 +93,63 @@ __global__ void __launch_bounds__(256) store_rows_self_kernel(const __grid_const
   }
 }
 
+// A big decode step's store: CTA c owns tokens [c T, c T + T) across every
+// plane (token-major), so it computes those T slots once (shared memory) and
+// reuses them for all 2L planes — with the plane-major order each token's
+// rows land in 2L different CTAs, each of which would compute its slot.  The
+// K/V reads stay contiguous within a plane.  Not a decode batch: it waits for
+// the index build and reads the slots, over the same rows.
+constexpr uint32_t kTokenMajorMaxTokens = 64;
+template <int W, int G, int VPL, int R, typename SlotT>
+__global__ void __launch_bounds__(256) store_tokens_self_kernel(const __grid_constant__ StoreParams p, uint32_t tpc) {
+  __shared__ int64_t s_slot[kTokenMajorMaxTokens];
+  const uint32_t lane = threadIdx.x % G;
+  const uint32_t lgroup = threadIdx.x / G;
+  const uint32_t step = (blockDim.x / G) * R;
+  const uint32_t N = p.by_tokens.d;
+  const uint32_t planes = p.total_rows / N;
+  const uint32_t t0 = blockIdx.x * tpc;
+  const uint32_t nt = t0 < N ? min(tpc, N - t0) : 0;
+  const uint32_t work = planes * nt;  // local row q: plane q / nt, token t0 + q % nt
+
+  RowBatch<W, G, VPL, R> b;
+  uint32_t rows[R];
+  bool ok[R];
+  auto pick = [&](uint32_t base) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint32_t q = base + r;
+      ok[r] = q < work;
+      const uint32_t plane = ok[r] ? q / nt : 0;
+      rows[r] = plane * N + t0 + (q - plane * nt);
+    }
+  };
+  uint32_t base = lgroup * R;
+  pick(base);
+  b.load_list(p, rows, ok, lane);
+  const bool self = decode_batch(p.self);
+  if (self) {
+    if (threadIdx.x < nt) s_slot[threadIdx.x] = decode_slot(p.self, t0 + threadIdx.x, p.error_word);
+    __syncthreads();  // uniform: self is the same on every thread
+  } else {
+    pdl_wait();
+  }
+  while (base < work) {
+    int64_t slot[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      slot[r] = !b.live[r] ? -1 : self ? s_slot[b.token[r] - t0] : load_slot<SlotT>(p.slots, b.token[r]);
+#pragma unroll
+    for (int r = 0; r < R; ++r) b.resolve(p, r, slot[r]);
+    b.store(lane);
+    base += step;
+    if (base < work) {
+      pick(base);
+      b.load_list(p, rows, ok, lane);
+    }
+  }
+}
+
 // TMA path: one CTA per SM stages its rows in shared memory.  The CTA owns a
 // contiguous range of rows; a round loads up to nslot of them with bulk
 // copies (thread t owns stage slots t, t + 256, ...), so at kernel start
@@ -218,10 +275,12 @@ __global__ void __launch_bounds__(256) store_rows_generic_kernel(const __grid_co
 // ---------------------------------------------------------------------------
 using StoreKernel = void (*)(StoreParams);
 
+using TokenKernel = void (*)(StoreParams, uint32_t);
 struct StoreVariant {
   StoreKernel fn;
   int group;  // lanes per row
   int rows;   // rows per group-iteration
+  TokenKernel tok = nullptr;  // the token-major kernel (fn unused)
 };
 
 int fast_vector_bytes() {
@@ -233,7 +292,7 @@ int fast_vector_bytes() {
 }
 
 // self: 0 the plain store, 1 the decode step's store computing slots per
-// row, 2 the same with the per-CTA slot cache.
+// row, 2 the same with the per-CTA slot cache, 3 the token-major store.
 static bool pick_fast(int64_t row_bytes, int w, bool slot64, int self, StoreVariant &out) {
   return dispatch_row_shape(row_bytes, w, [&](auto shape) {
     using S = decltype(shape);
@@ -245,6 +304,10 @@ static bool pick_fast(int64_t row_bytes, int w, bool slot64, int self, StoreVari
       out = StoreVariant{slot64 ? store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int64_t, true>
                                 : store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int32_t, true>,
                          S::G, S::R};
+    else if (self == 3)  // at most 4 rows per group (fewer registers: room beside the index build)
+      out = StoreVariant{nullptr, S::G, S::R > 4 ? 4 : S::R,
+                         slot64 ? store_tokens_self_kernel<S::W, S::G, S::VPL, (S::R > 4 ? 4 : S::R), int64_t>
+                                : store_tokens_self_kernel<S::W, S::G, S::VPL, (S::R > 4 ? 4 : S::R), int32_t>};
     else
       out = StoreVariant{slot64 ? store_rows_kernel<S::W, S::G, S::VPL, S::R, int64_t>
                                 : store_rows_kernel<S::W, S::G, S::VPL, S::R, int32_t>,
@@ -414,14 +477,39 @@ int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStre
   StoreVariant var{};
   bool fast = false;
   const int w = fast_vector_bytes();
-  const int self = plan.p.self.batch > 0 ? (plan.p.self.cached ? 2 : 1) : 0;
+  const int self = plan.p.self.batch > 0 ? 1 + plan.p.self.cached : 0;
   if (plan.unit == 16 && w == 32 && (plan.bits & 31u) == 0) fast = pick_fast(row_bytes, 32, slot64, self, var);
   if (!fast && plan.unit == 16) fast = pick_fast(row_bytes, 16, slot64, self, var);
   if (!fast) var = pick_generic(plan.unit, slot64);
   const uint64_t rows_per_block = static_cast<uint64_t>(kStoreThreads / var.group) * var.rows;
   const uint64_t want = (plan.p.total_rows + rows_per_block - 1) / rows_per_block;
+  if (var.tok != nullptr) {
+    // token-major: T tokens per CTA, as few as the resident CTAs allow
+    const uint64_t n = plan.p.by_tokens.d;
+    const uint64_t ctas = static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.tok), 0);
+    uint64_t tpc = (n + (ctas < n ? ctas : n) - 1) / (ctas < n ? ctas : n);
+    if (tpc > kTokenMajorMaxTokens) tpc = kTokenMajorMaxTokens;  // the host caps the batch so this does not bind
+    const unsigned grid = static_cast<unsigned>((n + tpc - 1) / tpc);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kStoreThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, var.tok, plan.p, static_cast<uint32_t>(tpc));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_last_error(std::string("yl_kv_store launch: ") + cudaGetErrorString(e));
+      return YL_ERR_CUDA;
+    }
+    return YL_OK;
+  }
   // the slot cache of a decode step's store
-  const size_t smem = fast && plan.p.self.cached ? static_cast<size_t>(plan.p.self.batch) * sizeof(int64_t) : 0;
+  const size_t smem = fast && plan.p.self.cached == 1 ? static_cast<size_t>(plan.p.self.batch) * sizeof(int64_t) : 0;
   const uint64_t cap =
       static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.fn), smem);
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);

@@ -29,7 +29,8 @@ struct SelfSlots {
   int32_t max_pages_per_row;
   int32_t num_table_rows;
   int32_t slot64;
-  int32_t cached;  // slots of all `batch` tokens computed once per CTA into shared memory (batch x 8 bytes)
+  int32_t cached;  // 0: a slot per row; 1: all `batch` slots once per CTA into shared memory (batch x 8
+                   // bytes); 2: the token-major kernel, each CTA its own tokens' slots
   FastDiv by_page;
 };
 
@@ -92,10 +93,20 @@ __device__ __forceinline__ void store_vec(char *p, const Vec<32> &x) {
 
 // True (on every thread of the block) when every sequence of the batch adds
 // exactly one token, so token t is sequence t's new token and the store can
-// compute slots itself.  Each thread reads its share of new_len.
+// compute slots itself.  Each thread reads its share of new_len, eight loads
+// in flight at a time.
 __device__ __forceinline__ bool decode_batch(const SelfSlots &s) {
   int ok = s.batch > 0;
-  for (int i = threadIdx.x; i < s.batch && ok; i += blockDim.x) ok = __ldg(s.new_len + i) == 1;
+  for (int base = threadIdx.x; base < s.batch; base += 8 * blockDim.x) {
+    int32_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * static_cast<int>(blockDim.x);
+      v[u] = i < s.batch ? __ldg(s.new_len + i) : 1;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ok &= v[u] == 1;
+  }
   return __syncthreads_and(ok) != 0;
 }
 
@@ -189,6 +200,21 @@ struct RowBatch {
       live[r] = row < p.total_rows;
       if (live[r]) {
         const RowAddr a = row_addr(p, row, token[r]);
+        dst[r] = a.dst_base;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) load_vec(data[r][j], a.src + (j * G + lane) * W);
+      }
+    }
+  }
+
+  // Issue the loads of the rows rows[r] for which ok[r] holds.
+  __device__ __forceinline__ void load_list(const StoreParams &p, const uint32_t (&rows)[R], const bool (&ok)[R],
+                                            uint32_t lane) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      live[r] = ok[r];
+      if (live[r]) {
+        const RowAddr a = row_addr(p, rows[r], token[r]);
         dst[r] = a.dst_base;
 #pragma unroll
         for (int j = 0; j < VPL; ++j) load_vec(data[r][j], a.src + (j * G + lane) * W);
