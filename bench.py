@@ -531,7 +531,10 @@ def run_ours(args, world, rank, local):
                          (args.workload, world)),
                      "peak_source": f"{peak_kind} hbm_gbs (copy)", "algorithmic_bytes_per_launch": store_bytes,
                      "launch_us": round(store_us, 3),
-                     "timing": f"{n_sep} back-to-back launches in one CUDA graph, events around the replays"},
+                     "timing": f"{n_sep} back-to-back launches in one CUDA graph, events around the replays",
+                     "timed_step_kernels": "build_index_kernel, then the store (for decode batches "
+                                           "store_rows_self_kernel / store_tokens_self_kernel, which compute "
+                                           "their own slots and run beside the index build)"},
         "gpu_launches": K * launches_per_step,
         "clocks": clocks.summary(),
     }
