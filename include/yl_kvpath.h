@@ -54,7 +54,7 @@ typedef enum yl_status {
   YL_ERR_NULL_ARG = -1,     /* a required pointer is NULL                        */
   YL_ERR_BAD_SIZE = -2,     /* negative count, zero/negative row size, ...       */
   YL_ERR_ALIGNMENT = -3,    /* pointer/stride not a multiple of the element unit */
-  YL_ERR_UNSUPPORTED = -4,  /* a combination this build does not implement       */
+  YL_ERR_UNSUPPORTED = -4,  /* a combination this library does not implement     */
   YL_ERR_CUDA = -5          /* the CUDA runtime refused the launch               */
 } yl_status;
 

@@ -1,8 +1,8 @@
 """Python face of the CPU oracle for the paged KV store and batch index build.
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, by ``__graft_entry__.smoke()``
-as the checker, and by bench.py's CPU-baseline leg.  The product package
-(``yllang_b200``) never imports it.
+to compare the GPU results against, and by bench.py's CPU-baseline leg.  The
+product package (``yllang_b200``) never imports it.
 
 Two restatements of the reference's algorithm live here:
 
@@ -48,7 +48,7 @@ _vp = ctypes.c_void_p
 
 
 def build(with_reference: bool = False) -> None:
-    """Compile the oracle (and, if asked and present, the reference checkers)."""
+    """Compile the oracle (and, if asked and present, the reference harnesses)."""
     target = ["all", "ref"] if with_reference else ["all"]
     env = dict(os.environ)
     # The C oracle is plain C11 + pthreads: any gcc works.

@@ -1,4 +1,4 @@
-// Reference checker and CPU baseline: the reference's own host index helper
+// Reference harness and CPU baseline: the reference's own host index helper
 // Make2DIndices (src/include/batch/batch_manager.h:30-51), compiled from the
 // reference source tree in place by oracle/Makefile, behind a C entry point.
 // TEST INFRASTRUCTURE ONLY.

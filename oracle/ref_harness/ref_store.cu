@@ -1,4 +1,4 @@
-// Parity checker: the reference's own StoreKVCache launcher and kernel
+// Parity harness: the reference's own StoreKVCache launcher and kernel
 // (src/kvcache/store_kv_cache.cu:46-163), compiled from the reference source
 // tree in place by oracle/Makefile, behind a C entry point that takes raw
 // device pointers.  TEST INFRASTRUCTURE ONLY.

@@ -1,6 +1,6 @@
 """Generate index-build golden vectors from the reference's own host code.
 
-Run in a tree where the reference checker oracle/_ref/libref_index.so has
+Run in a tree where the reference harness oracle/_ref/libref_index.so has
 been built (``make -C oracle ref``); writes tests/golden/index_ps1_*.json.
 
 The reference's only index code is Make2DIndices

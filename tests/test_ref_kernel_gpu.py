@@ -28,7 +28,7 @@ DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 
 @pytest.fixture(scope="module")
 def ref_store():
-    assert os.path.exists(REF_STORE), "reference checker not built (make -C oracle ref)"
+    assert os.path.exists(REF_STORE), "reference harness not built (make -C oracle ref)"
     L = ctypes.CDLL(REF_STORE)
     f = L.ref_store_kv_cache
     f.restype = ctypes.c_int
