@@ -242,6 +242,29 @@ def test_page_pool_empty_calls_are_noops_without_device():
     assert yl.lib().yl_release_pages(None, None) == _abi.YL_ERR_NULL_ARG
 
 
+def _header_defines(prefix):
+    text = open(HEADER).read()
+    return {m.group(1): int(m.group(2), 16) for m in re.finditer(rf"#define ({prefix}\w+)\s+(0x[0-9a-fA-F]+)u?", text)}
+
+
+def test_error_bits_and_statuses_agree_with_header():
+    """Every device error bit of the header has the same value in the Python
+    binding, and the oracle's bits are the header's; status codes likewise."""
+    from oracle import kvpath as orc
+
+    bits = _header_defines("YL_DEVERR_")
+    assert len(bits) >= 14 and len(set(bits.values())) == len(bits)
+    for name, value in bits.items():
+        short = name[len("YL_DEVERR_"):]
+        assert getattr(_abi, "DEVERR_" + short) == value, name
+        if hasattr(orc, short):
+            assert getattr(orc, short) == value, name
+    text = open(HEADER).read()
+    for m in re.finditer(r"(YL_(?:OK|ERR_\w+))\s*=\s*(-?\d+)", text):
+        assert getattr(_abi, m.group(1)) == int(m.group(2)), m.group(1)
+        assert _abi.status_string(int(m.group(2))) == m.group(1)
+
+
 def test_status_strings():
     assert _abi.status_string(0) == "YL_OK"
     assert _abi.status_string(-3) == "YL_ERR_ALIGNMENT"
