@@ -91,3 +91,45 @@ def test_table_rows_reserve_release_sync():
     assert torch.equal(m.PageTable(), m.HostPageTable())
     assert (m.HostPageTable()[rows[0]] == -1).all() and m.RemainingPageCount() == 64 - 1
     assert m.RemainingTableSlots() == 1
+
+
+def test_device_page_pool_rejects_bad_arguments():
+    with pytest.raises(C.PanicError, match="CUDA device"):
+        C.DevicePagePool(16, "cpu")
+    with pytest.raises(C.PanicError, match="num_pages"):
+        C.DevicePagePool(0, "cpu")
+
+
+def test_qk_norm_rope_options_defaults():
+    o = C.QKNormRope()
+    assert o.q_weight is None and o.k_weight is None and o.cos_sin_cache is None and o.positions is None
+    assert o.eps == pytest.approx(1e-6) and o.interleaved is False
+    o.eps, o.interleaved = 1e-5, True
+    assert o.eps == pytest.approx(1e-5) and o.interleaved is True
+
+
+def test_qk_norm_rope_store_kv_checks_before_any_launch():
+    """Shape and dtype contract first, then the device: CPU tensors are refused
+    (no host fallback)."""
+    q = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    k = torch.zeros(4, 1, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(8, 128, dtype=torch.bfloat16)
+    idx = torch.zeros(4, dtype=torch.int64)
+    with pytest.raises(C.PanicError, match="bf16 or fp16"):
+        C.QKNormRopeStoreKV(q.float(), k.float(), k.float(), kc.float(), kc.float(), idx, C.QKNormRope(), q.float())
+    with pytest.raises(C.PanicError, match="shapes"):
+        C.QKNormRopeStoreKV(q, k, k, kc, kc, idx, C.QKNormRope(), q[:3])
+    with pytest.raises(C.PanicError, match="contiguous heads"):
+        C.QKNormRopeStoreKV(q.transpose(1, 2), k, k, kc, kc, idx, C.QKNormRope(), q)
+    with pytest.raises(C.PanicError, match="CUDA tensors"):
+        C.QKNormRopeStoreKV(q, k, k, kc, kc, idx, C.QKNormRope(), q)
+
+
+def test_index_front_end_checks_before_any_launch():
+    w = torch.zeros(10, 64, dtype=torch.bfloat16)
+    with pytest.raises(C.PanicError, match="weights"):
+        C.Index(torch.zeros(3, dtype=torch.int32), w.t(), torch.zeros(3, 10, dtype=torch.bfloat16))
+    with pytest.raises(C.PanicError, match="destination"):
+        C.Index(torch.zeros(3, dtype=torch.int32), w, torch.zeros(3, 32, dtype=torch.bfloat16))
+    with pytest.raises(C.PanicError, match="CUDA tensors"):
+        C.Index(torch.zeros(3, dtype=torch.int32), w, torch.zeros(3, 64, dtype=torch.bfloat16))
