@@ -6,6 +6,7 @@ import ctypes
 import os
 import re
 import subprocess
+import sys
 
 import pytest
 
@@ -317,3 +318,22 @@ def test_fastdiv_exact(tmp_path):
     subprocess.run(["nvcc", "-std=c++17", "-O2", f"-I{csrc}", f"-I{os.path.dirname(HEADER)}", str(src), "-o",
                     str(exe)], check=True)
     assert subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.strip() == "0"
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """Without libyl_kvpath.so the package raises instead of falling back to
+    any host path (run in a child so this process keeps its library)."""
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "from yllang_b200 import _abi\n"
+        "_abi.LIB_PATH = %r\n"
+        "_abi._lib = None\n"
+        "try:\n"
+        "    _abi.lib()\n"
+        "except ImportError as e:\n"
+        "    print('refused:', e)\n"
+        "else:\n"
+        "    print('loaded')\n" % (ROOT, str(tmp_path / "libyl_kvpath.so"))
+    )
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.startswith("refused:") and "build the CUDA library" in r.stdout
