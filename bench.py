@@ -546,6 +546,8 @@ def run_ours(args, world, rank, local):
         line["qkv_norm_rope_store"] = bench_qkv(dev, peak)
     if not args.no_pool:
         line["page_allocator"] = bench_pool(dev)
+    if not args.no_make2d:
+        line["make2dindices"] = bench_make2d(dev, b0, peak)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_store_step_sample(b0, seconds=args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -573,6 +575,35 @@ def bench_gather(dev, peak: float, tokens: int = 4096, sets: int = 32) -> dict:
     return {"workload": f"qwen3-0.6b token embedding {V}x{E} bf16, {tokens} ids (int32)", "us_per_launch": round(us, 3),
             "algorithmic_bytes_per_launch": nbytes, "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
             "kernel": "gather_rows_kernel", "timing": "256 back-to-back launches in one CUDA graph; table rows may hit L2"}
+
+
+def bench_make2d(dev, b: workloads.Batch, peak: float, sets: int = 4) -> dict:
+    """The reference's Make2DIndices on the decode batch's load ranges
+    ({row * W, 0, prior + new} per sequence: one index per context token, as
+    NextBatch calls it at page size 1), one yl_make_2d_indices launch each,
+    outputs rotating over `sets` buffers.  Algorithmic bytes per launch: the
+    ranges read + the int64 indices written."""
+    tot = b.prior_len.astype(np.int64) + b.new_len
+    W = int(tot.max())
+    r = np.stack([np.arange(b.batch, dtype=np.int64) * W, np.zeros(b.batch, np.int64), tot], axis=1)
+    ranges = torch.from_numpy(np.ascontiguousarray(r)).to(dev)
+    n = int(tot.sum())
+    outs = [torch.empty(n, dtype=torch.int64, device=dev) for _ in range(sets)]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    yl.make_2d_indices(ranges, out=outs[0], error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    last = (b.batch - 1) * W + torch.arange(int(tot[-1]), device=dev)
+    assert torch.equal(outs[0][:int(tot[0])], torch.arange(int(tot[0]), device=dev))
+    assert torch.equal(outs[0][n - int(tot[-1]):], last)
+    us = per_launch_us(sets, lambda j: [lambda: yl.make_2d_indices(ranges, out=outs[j], error_word=err)], 256)
+    nbytes = b.batch * 24 + n * 8
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": f"{b.name} load ranges: {b.batch} ranges, {n} indices (int64)", "us_per_batch": round(us, 3),
+            "algorithmic_bytes_per_launch": nbytes, "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+            "kernel": "make_2d_indices_kernel",
+            "timing": f"256 back-to-back launches in one CUDA graph, outputs rotating over {sets} buffers "
+                      f"({sets * n * 8 / 1e6:.0f} MB, may stay in L2)"}
 
 
 def bench_qkv(dev, peak: float) -> dict:
@@ -826,6 +857,7 @@ def main():
     ap.add_argument("--no-gather", action="store_true", help="skip the embedding-gather line")
     ap.add_argument("--no-qkv", action="store_true", help="skip the fused norm/rotary/store line")
     ap.add_argument("--no-pool", action="store_true", help="skip the page-allocator line")
+    ap.add_argument("--no-make2d", action="store_true", help="skip the range-expansion (Make2DIndices) line")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

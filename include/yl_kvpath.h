@@ -62,14 +62,14 @@ typedef enum yl_status {
 #define YL_DEVERR_SLOT_RANGE      0x1u  /* store: slot >= num_slots or < -1 (row skipped)   */
 #define YL_DEVERR_PAGE_RANGE      0x2u  /* index: page id outside [0, num_pages)            */
 #define YL_DEVERR_ROW_OVERFLOW    0x4u  /* index: a sequence needs more pages than its row  */
-#define YL_DEVERR_INDICES_CAP     0x8u  /* index: sum of pages exceeds kv_indices_capacity  */
+#define YL_DEVERR_INDICES_CAP     0x8u  /* index, ranges: output exceeds its capacity       */
 #define YL_DEVERR_SLOTS_CAP       0x10u /* index: sum of new tokens exceeds slot_capacity   */
-#define YL_DEVERR_NEGATIVE_LEN    0x20u /* index: a negative length (treated as 0)          */
+#define YL_DEVERR_NEGATIVE_LEN    0x20u /* index, ranges: a negative length (treated as 0)  */
 #define YL_DEVERR_INDPTR_OVERFLOW 0x40u /* index: a running sum passed INT32_MAX (no fill)  */
 #define YL_DEVERR_TABLE_ROW       0x80u /* index: table_index outside [0, num_table_rows)   */
 #define YL_DEVERR_TOKEN_COUNT     0x100u /* step: sum of new_len differs from num_tokens      */
 #define YL_DEVERR_TIMEOUT         0x200u /* store: a bulk copy did not complete within 2 s    */
-#define YL_DEVERR_INDEX_RANGE     0x400u /* gather: index outside [-1, num_rows)              */
+#define YL_DEVERR_INDEX_RANGE     0x400u /* gather: index outside [-1, num_rows); ranges: index past INT64_MAX */
 #define YL_DEVERR_POSITION_RANGE  0x800u /* qkv store: position outside [0, max_position)     */
 #define YL_DEVERR_POOL_EMPTY      0x1000u /* reserve: fewer free pages than the batch needs  */
 #define YL_DEVERR_POOL_OVERFLOW   0x2000u /* release: more pages than the free list holds    */
@@ -348,6 +348,31 @@ typedef struct yl_release_args {
 } yl_release_args;
 
 YL_API int yl_release_pages(const yl_release_args *args, cudaStream_t stream);
+
+/*
+ * Range expansion (replaces Make2DIndices, src/include/batch/batch_manager.h:30-51,
+ * the helper NextBatch calls to turn {row, col_start, col_end} ranges into flat
+ * page-table indices, batch_manager.h:97-107): for each range r in order,
+ *     indices <- row_r + c   for c in [col_start_r, col_end_r)
+ * concatenated, as int64 (the reference returns a default float tensor,
+ * batch_manager.h:38, exact only below 2^24).  As in the reference, the row
+ * entry is added as given: a caller that wants row-major flat indices passes
+ * row * row_stride.  A range with a negative entry or col_end < col_start adds
+ * nothing and sets YL_DEVERR_NEGATIVE_LEN; one whose last index would pass
+ * INT64_MAX adds nothing and sets YL_DEVERR_INDEX_RANGE.  Indices past
+ * indices_capacity are not written and set YL_DEVERR_INDICES_CAP; *count (when
+ * given) receives the full total, so a caller can size the output first.
+ */
+typedef struct yl_ranges_args {
+  const int64_t *ranges;      /* [num_ranges, 3] int64: row, col_start, col_end   */
+  int64_t *indices;           /* [indices_capacity] int64 output                   */
+  int64_t *count;             /* optional [1]: total indices of the valid ranges   */
+  int64_t num_ranges;         /* <= 2^22                                           */
+  int64_t indices_capacity;   /* < 2^40                                            */
+  uint32_t *error_word;
+} yl_ranges_args;
+
+YL_API int yl_make_2d_indices(const yl_ranges_args *args, cudaStream_t stream);
 
 /* Human-readable name of a yl_status value (static storage). */
 YL_API const char *yl_status_string(int status);

@@ -78,6 +78,8 @@ def lib() -> ctypes.CDLL:
                                            ctypes.c_int32, ctypes.c_int32]
         L.oracle_gather_rows.restype = _i64
         L.oracle_gather_rows.argtypes = [_vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _vp]
+        L.oracle_make_2d_indices.restype = ctypes.c_uint32
+        L.oracle_make_2d_indices.argtypes = [_vp, _i64, _vp, _i64, _vp]
         _lib = L
     return _lib
 
@@ -169,6 +171,21 @@ def gather(indices: np.ndarray, table: np.ndarray, num_rows: int | None = None) 
                                  table.shape[1] * table.itemsize, table.strides[0], out.strides[0],
                                  table.shape[0] if num_rows is None else num_rows, ctypes.addressof(err))
     return out, int(err.value)
+
+
+def make_2d_indices(ranges, capacity: int | None = None) -> tuple[np.ndarray, int, int]:
+    """Make2DIndices (batch_manager.h:30-51) over {row, col_start, col_end}
+    ranges: returns (the first min(total, capacity) indices as int64, total,
+    error bits); capacity None means room for all of them."""
+    r = np.ascontiguousarray(np.asarray(ranges, np.int64).reshape(-1, 3))
+    count = ctypes.c_int64(0)
+    if capacity is None:
+        lib().oracle_make_2d_indices(_ptr(r), r.shape[0], None, 0, ctypes.addressof(count))
+        capacity = int(count.value)
+    out = np.zeros(max(capacity, 1), np.int64)
+    err = lib().oracle_make_2d_indices(_ptr(r), r.shape[0], _ptr(out), capacity, ctypes.addressof(count))
+    total = int(count.value)
+    return out[:min(total, capacity)].copy(), total, int(err)
 
 
 class PagePool:
@@ -289,6 +306,15 @@ def py_store(k, v, k_cache, v_cache, slots) -> None:
                 continue
             kc3[layer, s] = k3[layer, i]
             vc3[layer, s] = v3[layer, i]
+
+
+def py_make_2d_indices(ranges) -> np.ndarray:
+    """Make2DIndices as written (batch_manager.h:40-47), valid ranges only:
+    row + start .. row + end - 1 for every range, in order."""
+    out = []
+    for row, start, end in np.asarray(ranges, np.int64).reshape(-1, 3).tolist():
+        out += range(row + start, row + end)
+    return np.array(out, np.int64)
 
 
 def py_build_index(prior_len, new_len, page_table, page_size, table_index=None):

@@ -315,6 +315,32 @@ uint32_t oracle_release_pages(int32_t *free_pages, int32_t *free_count, int64_t 
   return 0;
 }
 
+/*
+ * Range expansion, following Make2DIndices (src/include/batch/batch_manager.h:30-51):
+ * for each range {row, col_start, col_end} in order, the indices
+ * row + col_start .. row + col_end - 1 (batch_manager.h:42-47), concatenated,
+ * as int64 instead of the helper's float.  Validation as in yl_make_2d_indices:
+ * a negative entry or col_end < col_start adds nothing (bit 0x20); row +
+ * col_end past INT64_MAX adds nothing (bit 0x400); lengths count at most 2^40;
+ * indices past `capacity` are not written (bit 0x8).  *count gets the total.
+ */
+uint32_t oracle_make_2d_indices(const int64_t *ranges, int64_t num_ranges, int64_t *out, int64_t capacity,
+                                int64_t *count) {
+  uint32_t err = 0;
+  int64_t pos = 0;
+  for (int64_t r = 0; r < num_ranges; ++r) {
+    const int64_t row = ranges[3 * r], lo = ranges[3 * r + 1], hi = ranges[3 * r + 2];
+    if (row < 0 || lo < 0 || hi < lo) { err |= ORACLE_NEGATIVE_LEN; continue; }
+    if (row > INT64_MAX - hi) { err |= ORACLE_INDEX_RANGE; continue; }
+    const int64_t len = hi - lo < ((int64_t)1 << 40) ? hi - lo : ((int64_t)1 << 40);
+    for (int64_t c = 0; c < len && pos + c < capacity; ++c) out[pos + c] = row + lo + c;
+    pos += len;
+  }
+  if (pos > capacity) err |= ORACLE_INDICES_CAP;
+  if (count) *count = pos;
+  return err;
+}
+
 /* Host threads available to this process (online processors). */
 int oracle_max_threads(void) {
   const long n = sysconf(_SC_NPROCESSORS_ONLN);

@@ -1,7 +1,9 @@
 """Generate index-build golden vectors from the reference's own host code.
 
 Run in a tree where the reference harness oracle/_ref/libref_index.so has
-been built (``make -C oracle ref``); writes tests/golden/index_ps1_*.json.
+been built (``make -C oracle ref``); writes tests/golden/index_ps1_*.json and
+tests/golden/make2d_ranges.json (the helper's own output for multi-range
+calls).
 
 The reference's only index code is Make2DIndices
 (src/include/batch/batch_manager.h:30-51), which NextBatch calls with one
@@ -80,6 +82,28 @@ def case(f, name, page_table, table_index, cached, device):
     return doc
 
 
+def make2d_cases(f):
+    """Make2DIndices calls as NextBatch makes them (one {row, cached, device}
+    range per request, all requests in one call), with the row entries as
+    given (the helper adds them without a row stride) and as row * W."""
+    rng = np.random.default_rng(11)
+    calls = []
+    for n, W, scale in ((1, 64, 1), (5, 128, 1), (5, 128, 0), (37, 512, 1), (700, 96, 1)):
+        rows = rng.permutation(max(n, 8))[:n]
+        cached = rng.integers(0, W // 2, n)
+        device = cached + rng.integers(0, W // 2, n)
+        if n > 3:
+            device[1] = cached[1]          # an empty range
+            cached[2], device[2] = 0, 0    # another
+        ranges = np.stack([rows * (W if scale else 1), cached, device], axis=1).astype(np.int64)
+        out = make2d(f, max(n, 8), W, ranges)
+        calls.append({"ranges": ranges.tolist(), "indices": out.tolist()})
+    doc = {"source": "reference Make2DIndices (src/include/batch/batch_manager.h:30-51) via oracle/_ref/libref_index.so",
+           "calls": calls}
+    with open(os.path.join(HERE, "make2d_ranges.json"), "w") as fh:
+        json.dump(doc, fh, separators=(",", ":"))
+
+
 def main():
     f = _ref()
     # The five requests of the 1-layer CPU config at page size 1: cached
@@ -100,6 +124,7 @@ def main():
     cached[5], extend[5] = 0, 0
     device = cached + extend
     case(f, "ragged_permuted_rows", table, rows, cached, device)
+    make2d_cases(f)
 
 
 if __name__ == "__main__":

@@ -51,7 +51,8 @@ def _c_layout(tmp_path, struct, fields):
 @pytest.mark.parametrize("struct,cls", [("yl_store_args", _abi.StoreArgs), ("yl_index_args", _abi.IndexArgs),
                                         ("yl_step_args", _abi.StepArgs), ("yl_gather_args", _abi.GatherArgs),
                                         ("yl_qkv_store_args", _abi.QkvStoreArgs), ("yl_page_pool", _abi.PagePool),
-                                        ("yl_reserve_args", _abi.ReserveArgs), ("yl_release_args", _abi.ReleaseArgs)])
+                                        ("yl_reserve_args", _abi.ReserveArgs), ("yl_release_args", _abi.ReleaseArgs),
+                                        ("yl_ranges_args", _abi.RangesArgs)])
 def test_struct_layout_matches_header(tmp_path, struct, cls):
     names = [f for f, _ in cls._fields_]
     c = _c_layout(tmp_path, struct, names)
@@ -241,6 +242,36 @@ def test_page_pool_empty_calls_are_noops_without_device():
     assert _abi.reserve_pages_raw(_pool_args(_abi.ReserveArgs, new_len=0), None) == _abi.YL_ERR_NULL_ARG
     assert yl.lib().yl_reserve_pages(None, None) == _abi.YL_ERR_NULL_ARG
     assert yl.lib().yl_release_pages(None, None) == _abi.YL_ERR_NULL_ARG
+
+
+def _ranges(**kw):
+    a = _abi.RangesArgs()
+    base = dict(ranges=0x10000, indices=0x20000, count=0x30000, num_ranges=4, indices_capacity=100, error_word=0x40000)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(num_ranges=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(indices_capacity=-1), _abi.YL_ERR_BAD_SIZE),
+    (dict(num_ranges=(1 << 22) + 1), _abi.YL_ERR_UNSUPPORTED),
+    (dict(indices_capacity=1 << 40), _abi.YL_ERR_UNSUPPORTED),
+    (dict(ranges=0), _abi.YL_ERR_NULL_ARG),
+    (dict(indices=0), _abi.YL_ERR_NULL_ARG),
+    (dict(ranges=0x10004), _abi.YL_ERR_ALIGNMENT),
+    (dict(indices=0x20002), _abi.YL_ERR_ALIGNMENT),
+    (dict(count=0x30001), _abi.YL_ERR_ALIGNMENT),
+])
+def test_make_2d_indices_rejects_bad_arguments_on_host(kw, status):
+    assert _abi.make_2d_indices_raw(_ranges(**kw), None) == status
+    assert _abi.last_error().startswith("yl_make_2d_indices")
+
+
+def test_make_2d_indices_empty_call_is_noop_without_device():
+    assert _abi.make_2d_indices_raw(_ranges(num_ranges=0, count=0, ranges=0, indices=0), None) == _abi.YL_OK
+    assert yl.lib().yl_make_2d_indices(None, None) == _abi.YL_ERR_NULL_ARG
 
 
 def _header_defines(prefix):

@@ -133,3 +133,11 @@ def test_index_front_end_checks_before_any_launch():
         C.Index(torch.zeros(3, dtype=torch.int32), w, torch.zeros(3, 32, dtype=torch.bfloat16))
     with pytest.raises(C.PanicError, match="CUDA tensors"):
         C.Index(torch.zeros(3, dtype=torch.int32), w, torch.zeros(3, 64, dtype=torch.bfloat16))
+
+
+def test_make_2d_indices_front_end_checks_before_any_launch():
+    r = [torch.tensor([0, 1, 3])]
+    with pytest.raises(C.PanicError, match="2-D"):
+        C.Make2DIndices(torch.zeros(4), r)
+    with pytest.raises(C.PanicError, match="CUDA"):
+        C.Make2DIndices(torch.zeros(4, 8), r)

@@ -2,6 +2,8 @@
 
 * index build vs golden vectors produced by the reference's own
   Make2DIndices (tests/golden/index_ps1_*.json, made by make_index_golden.py);
+* range expansion vs that helper's own output for multi-range calls
+  (tests/golden/make2d_ranges.json, same script);
 * index build vs the known answers of the five-request page-size-16 batch;
 * C oracle vs the independent pure-Python restatement on seeded random cases;
 * store semantics ported from the reference's test/mha_kvcache_test.cpp.
@@ -31,6 +33,32 @@ def test_index_oracle_matches_reference_make2dindices(path):
     # page size 1: every non-empty sequence's last page holds one token
     tot = np.array(d["prior_len"]) + np.array(d["new_len"])
     assert out["kv_last_page_len"].tolist() == [1 if t else 0 for t in tot]
+
+
+def test_make2d_oracle_matches_reference_make2dindices():
+    d = json.load(open(os.path.join(GOLDEN, "make2d_ranges.json")))
+    assert len(d["calls"]) >= 5
+    for call in d["calls"]:
+        out, total, bits = orc.make_2d_indices(call["ranges"])
+        assert bits == 0 and total == len(call["indices"])
+        assert out.tolist() == call["indices"]
+        assert orc.py_make_2d_indices(call["ranges"]).tolist() == call["indices"]
+
+
+def test_make2d_oracle_edge_cases():
+    empty, total, bits = orc.make_2d_indices(np.zeros((0, 3), np.int64))
+    assert empty.size == 0 and total == 0 and bits == 0
+    out, total, bits = orc.make_2d_indices([[10, 2, 5], [0, 4, 4], [100, 0, 2]])
+    assert out.tolist() == [12, 13, 14, 100, 101] and bits == 0
+    # a negative entry or an inverted range adds nothing
+    out, total, bits = orc.make_2d_indices([[-1, 0, 3], [7, 5, 2], [1, 0, 2]])
+    assert out.tolist() == [1, 2] and bits == orc.NEGATIVE_LEN
+    # row + col_end past INT64_MAX adds nothing
+    out, total, bits = orc.make_2d_indices([[2**63 - 2, 0, 5], [3, 0, 1]])
+    assert out.tolist() == [3] and bits == orc.INDEX_RANGE
+    # capacity: the first `capacity` indices, the total, the bit
+    out, total, bits = orc.make_2d_indices([[0, 0, 4], [50, 0, 4]], capacity=6)
+    assert out.tolist() == [0, 1, 2, 3, 50, 51] and total == 8 and bits == orc.INDICES_CAP
 
 
 def test_index_oracle_known_answers_page16():

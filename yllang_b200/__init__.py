@@ -13,6 +13,8 @@ The hot path of one YLLang serving step, rebuilt for sm_100a:
   Index) on the same copy engine;
 * ``qkv_norm_rope_store`` / ``yl_qkv_norm_rope_store``: one layer's Q/K
   RMSNorm and rotary embedding fused with the K/V store;
+* ``make_2d_indices`` / ``yl_make_2d_indices``: the flat page-table indices
+  of {row, col_start, col_end} ranges (YLLang's Make2DIndices);
 * ``DevicePagePool`` / ``yl_reserve_pages``, ``yl_release_pages``: the
   free-page list and page-table updates of YLLang's KVCacheManager on the
   device, feeding the index build without a host round trip.
@@ -27,11 +29,12 @@ from ._abi import (DEVERR_INDICES_CAP, DEVERR_INDPTR_OVERFLOW, DEVERR_NEGATIVE_L
                    DEVERR_INDEX_RANGE, DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW,
                    DEVERR_POOL_EMPTY, DEVERR_POOL_OVERFLOW, DEVERR_POSITION_RANGE, DEVERR_TIMEOUT, DEVERR_TOKEN_COUNT,
                    KVPathError, lib)
-from .ops import (BatchIndex, DevicePagePool, PanicError, build_index, gather_rows, kv_step, qkv_norm_rope_store,
-                  rope_cos_sin_cache, store_args, store_kv_cache)
+from .ops import (BatchIndex, DevicePagePool, PanicError, build_index, gather_rows, kv_step, make_2d_indices,
+                  qkv_norm_rope_store, rope_cos_sin_cache, store_args, store_kv_cache)
 
 __all__ = [
-    "BatchIndex", "DevicePagePool", "KVPathError", "PanicError", "build_index", "gather_rows", "kv_step", "qkv_norm_rope_store",
+    "BatchIndex", "DevicePagePool", "KVPathError", "PanicError", "build_index", "gather_rows", "kv_step", "make_2d_indices",
+    "qkv_norm_rope_store",
     "rope_cos_sin_cache", "store_args", "store_kv_cache", "lib",
     "load_extension", "DEVERR_SLOT_RANGE", "DEVERR_PAGE_RANGE", "DEVERR_ROW_OVERFLOW", "DEVERR_INDICES_CAP",
     "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW", "DEVERR_TOKEN_COUNT",

@@ -194,9 +194,24 @@ class ReleaseArgs(ctypes.Structure):
         ("error_word", _vp),
     ]
 
+
+class RangesArgs(ctypes.Structure):
+    """struct yl_ranges_args."""
+
+    _fields_ = [
+        ("ranges", _vp),
+        ("indices", _vp),
+        ("count", _vp),
+        ("num_ranges", _i64),
+        ("indices_capacity", _i64),
+        ("error_word", _vp),
+    ]
+
+
 # Every symbol include/yl_kvpath.h declares.
 EXPORTED_SYMBOLS = ("yl_kv_store", "yl_build_index", "yl_kv_step", "yl_gather_rows", "yl_qkv_norm_rope_store",
-                    "yl_reserve_pages", "yl_release_pages", "yl_status_string", "yl_last_error", "yl_abi_version")
+                    "yl_reserve_pages", "yl_release_pages", "yl_make_2d_indices", "yl_status_string", "yl_last_error",
+                    "yl_abi_version")
 
 _lib: ctypes.CDLL | None = None
 
@@ -232,6 +247,8 @@ def lib() -> ctypes.CDLL:
         L.yl_reserve_pages.argtypes = [ctypes.POINTER(ReserveArgs), _vp]
         L.yl_release_pages.restype = ctypes.c_int
         L.yl_release_pages.argtypes = [ctypes.POINTER(ReleaseArgs), _vp]
+        L.yl_make_2d_indices.restype = ctypes.c_int
+        L.yl_make_2d_indices.argtypes = [ctypes.POINTER(RangesArgs), _vp]
         L.yl_status_string.restype = ctypes.c_char_p
         L.yl_status_string.argtypes = [ctypes.c_int]
         L.yl_last_error.restype = ctypes.c_char_p
@@ -283,3 +300,7 @@ def reserve_pages_raw(args: ReserveArgs, stream: int | None) -> int:
 
 def release_pages_raw(args: ReleaseArgs, stream: int | None) -> int:
     return lib().yl_release_pages(ctypes.byref(args), stream)
+
+
+def make_2d_indices_raw(args: RangesArgs, stream: int | None) -> int:
+    return lib().yl_make_2d_indices(ctypes.byref(args), stream)

@@ -24,7 +24,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libyl_kvpath.so")
 
 CUDA_SOURCES = ["common.cu", "kv_store.cu", "index_build.cu", "kv_step.cu", "gather.cu", "qkv_store.cu",
-                "page_alloc.cu"]
+                "page_alloc.cu", "ranges.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -115,6 +115,9 @@ PYBIND11_MODULE(_C, m) {
       py::arg("prior_len"), py::arg("new_len"), py::arg("page_table"), py::arg("page_size"),
       py::arg("table_index") = py::none(), py::arg("num_pages") = 0, py::arg("kv_indices_capacity") = -1,
       py::arg("slot_capacity") = -1, py::arg("slot_int64") = true, py::arg("error_word") = py::none());
+  m.def("Make2DIndices", &Make2DIndices, py::arg("table"), py::arg("ranges"),
+        "flat indices row + c, c in [col_start, col_end), of {row, col_start, col_end} ranges (int64, on the "
+        "table's device)");
 
   py::class_<KVCacheManager, std::shared_ptr<KVCacheManager>>(m, "KVCacheManager")
       .def(py::init([](int64_t num_pages, int64_t max_requests, int64_t max_pages_per_request, int page_size,

@@ -7,6 +7,7 @@
 #include <c10/core/DeviceGuard.h>
 
 #include <algorithm>
+#include <climits>
 #include <numeric>
 #include <sstream>
 
@@ -409,6 +410,44 @@ BatchIndex BuildBatchIndex(const torch::Tensor &prior_len, const torch::Tensor &
   }
   const c10::cuda::CUDAGuard guard(prior_len.device());
   CheckStatus(yl_build_index(&a, CurrentStream(prior_len)), "yl_build_index");
+  return out;
+}
+
+// ----------------------------------------------------------------------------
+torch::Tensor Make2DIndices(const torch::Tensor &table, const std::vector<torch::Tensor> &ranges) {
+  RuntimeCheck(table.dim() == 2, "Make2DIndices: table must be 2-D");
+  RuntimeCheck(table.is_cuda(), "Make2DIndices: table must be a CUDA tensor (the indices are made on its device)");
+  const int64_t R = static_cast<int64_t>(ranges.size());
+  std::vector<torch::Tensor> firsts;
+  firsts.reserve(ranges.size());
+  for (const auto &r : ranges) {
+    RuntimeCheck(r.numel() >= 3, "Make2DIndices: each range needs three entries {row, col_start, col_end}");
+    RuntimeCheck(r.device() == ranges.front().device(), "Make2DIndices: ranges on different devices");
+    firsts.push_back(r.reshape({-1}).narrow(0, 0, 3).to(torch::kInt64));
+  }
+  const torch::Tensor host = R ? torch::stack(firsts).to(torch::kCPU).contiguous()
+                               : torch::empty({0, 3}, torch::dtype(torch::kInt64));
+  const int64_t *h = host.data_ptr<int64_t>();
+  int64_t total = 0;
+  for (int64_t i = 0; i < R; ++i) {
+    const int64_t row = h[3 * i], lo = h[3 * i + 1], hi = h[3 * i + 2];
+    RuntimeCheck(row >= 0 && lo >= 0 && hi >= lo,
+                 "Make2DIndices: a range needs row >= 0, col_start >= 0 and col_end >= col_start");
+    RuntimeCheck(row <= INT64_MAX - hi, "Make2DIndices: row + col_end passes INT64_MAX");
+    total += hi - lo;
+    RuntimeCheck(total < (int64_t{1} << 40), "Make2DIndices: more than 2^40 indices");
+  }
+  const auto opts = torch::TensorOptions().dtype(torch::kInt64).device(table.device());
+  torch::Tensor out = torch::empty({total}, opts);
+  if (total == 0) return out;
+  const c10::cuda::CUDAGuard guard(table.device());
+  const torch::Tensor dev_ranges = host.to(table.device());
+  yl_ranges_args a{};
+  a.ranges = dev_ranges.data_ptr<int64_t>();
+  a.indices = out.data_ptr<int64_t>();
+  a.num_ranges = R;
+  a.indices_capacity = total;
+  CheckStatus(yl_make_2d_indices(&a, CurrentStream(table)), "yl_make_2d_indices");
   return out;
 }
 

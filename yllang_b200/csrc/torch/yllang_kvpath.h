@@ -192,6 +192,15 @@ BatchIndex BuildBatchIndex(const torch::Tensor &prior_len, const torch::Tensor &
                            torch::Dtype slot_dtype = torch::kInt64,
                            const std::optional<torch::Tensor> &error_word = std::nullopt);
 
+// Make2DIndices (src/include/batch/batch_manager.h:30-51): for each range
+// {row, col_start, col_end} (the first three entries of each tensor, read on
+// the host as the reference does), the indices row + c for c in
+// [col_start, col_end), concatenated.  Made on the table's device as int64
+// (the reference returns a CPU float tensor); the table is otherwise unused,
+// as in the reference.  A negative entry or col_end < col_start throws
+// PanicError (the reference's size_t arithmetic wraps there).
+torch::Tensor Make2DIndices(const torch::Tensor &table, const std::vector<torch::Tensor> &ranges);
+
 // ----------------------------------------------------------------------------
 // Page allocator + page table (host free lists, device page table)
 // ----------------------------------------------------------------------------

@@ -246,6 +246,50 @@ def gather_rows(indices: torch.Tensor, table: torch.Tensor, out: torch.Tensor | 
     return out
 
 
+def make_2d_indices(ranges: torch.Tensor, out: torch.Tensor | None = None, count: torch.Tensor | None = None,
+                    error_word: torch.Tensor | None = None,
+                    stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Flat indices of {row, col_start, col_end} ranges: row + c for c in
+    [col_start, col_end), range after range (Make2DIndices,
+    src/include/batch/batch_manager.h:30-51, as int64 instead of float).
+
+    ranges: device int64 [R, 3].  With ``out`` (device int64 [capacity]) the
+    call never leaves the device: indices past the capacity are dropped and
+    flagged (DEVERR_INDICES_CAP), and ``count`` (device int64 [1]) receives the
+    total.  Without ``out`` the total is computed here from the ranges (one
+    copy to the host), invalid ranges raise PanicError, and a tensor of exactly
+    that length is returned."""
+    _check(ranges.is_cuda, "ranges must be a CUDA tensor")
+    _check(ranges.dtype == torch.int64, f"ranges dtype {ranges.dtype} must be int64")
+    _check(ranges.dim() == 2 and ranges.shape[1] == 3, f"ranges must be [R, 3], got {tuple(ranges.shape)}")
+    _check(ranges.is_contiguous(), "ranges must be contiguous")
+    dev = ranges.device
+    if out is None:
+        host = ranges.cpu()
+        row, lo, hi = host[:, 0], host[:, 1], host[:, 2]
+        _check(bool((row >= 0).all() and (lo >= 0).all() and (hi >= lo).all()),
+               "ranges need row >= 0, col_start >= 0 and col_end >= col_start")
+        _check(all(r <= (1 << 63) - 1 - h for r, h in zip(row.tolist(), hi.tolist())),
+               "ranges: row + col_end passes INT64_MAX")
+        total = sum((hi - lo).tolist())
+        _check(total < (1 << 40), f"ranges: {total} indices is not below 2^40")
+        out = torch.empty(total, dtype=torch.int64, device=dev)
+    _check(out.dtype == torch.int64 and out.dim() == 1 and out.is_contiguous() and out.device == dev,
+           "out must be a contiguous int64 [capacity] tensor on the ranges' device")
+    if count is not None:
+        _check(count.dtype == torch.int64 and count.numel() >= 1 and count.device == dev,
+               "count must be an int64 tensor on the ranges' device")
+    a = _abi.RangesArgs()
+    a.ranges = ranges.data_ptr() if ranges.numel() else None
+    a.indices = out.data_ptr() if out.numel() else None
+    a.count = count.data_ptr() if count is not None else None
+    a.num_ranges = ranges.shape[0]
+    a.indices_capacity = out.numel()
+    a.error_word = error_word.data_ptr() if error_word is not None else None
+    _abi.check(_abi.make_2d_indices_raw(a, _stream(stream, dev)))
+    return out
+
+
 def rope_cos_sin_cache(max_position: int, head_dim: int, theta: float = 1e6,
                        device: torch.device | str = "cpu") -> torch.Tensor:
     """[max_position, head_dim] fp32: head_dim / 2 cosines then head_dim / 2
