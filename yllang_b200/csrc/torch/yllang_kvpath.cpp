@@ -6,6 +6,8 @@
 #include <c10/cuda/CUDAStream.h>
 #include <c10/core/DeviceGuard.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
 #include <climits>
 #include <numeric>
@@ -20,6 +22,17 @@ void RuntimeCheck(bool cond, const std::string &msg) {
 }
 
 namespace {
+
+// NVTX range over one front-end call, so a profiler timeline (nsys, or ncu's
+// --nvtx range filters) shows which call launched which kernels; costs a
+// function-pointer check when no tool is attached.
+class Range {
+ public:
+  explicit Range(const char *name) { nvtxRangePushA(name); }
+  ~Range() { nvtxRangePop(); }
+  Range(const Range &) = delete;
+  Range &operator=(const Range &) = delete;
+};
 
 void CheckStatus(int status, const char *what) {
   if (status != YL_OK) {
@@ -86,6 +99,7 @@ void CheckIndices(const torch::Tensor &indices, int64_t n, const torch::Tensor &
 
 void StoreKVCache(const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &k_cache,
                   const torch::Tensor &v_cache, const torch::Tensor &indices) {
+  const Range range("yllang::StoreKVCache");
   // TensorMatcher contract of store_kv_cache.cu:108-124
   RuntimeCheck(k_cache.dim() == 2 && v_cache.dim() == 2, "StoreKVCache: caches must be [S, E]");
   RuntimeCheck(k.dim() == 2 && v.dim() == 2, "StoreKVCache: k and v must be [N, E]");
@@ -102,6 +116,7 @@ void StoreKVCache(const torch::Tensor &k, const torch::Tensor &v, const torch::T
 
 void StoreKVCacheLayers(const torch::Tensor &k, const torch::Tensor &v, const torch::Tensor &k_cache,
                         const torch::Tensor &v_cache, const torch::Tensor &indices) {
+  const Range range("yllang::StoreKVCacheLayers");
   RuntimeCheck(k.dim() == 3 && v.dim() == 3, "StoreKVCacheLayers: k and v must be [L, N, E]");
   RuntimeCheck(k_cache.dim() == 3 && v_cache.dim() == 3, "StoreKVCacheLayers: caches must be [L, S, E]");
   RuntimeCheck(k.sizes() == v.sizes(), "StoreKVCacheLayers: k and v differ in shape");
@@ -117,6 +132,7 @@ void StoreKVCacheLayers(const torch::Tensor &k, const torch::Tensor &v, const to
 }
 
 void Index(const torch::Tensor &indices, const torch::Tensor &weights, const torch::Tensor &destination) {
+  const Range range("yllang::Index");
   RuntimeCheck(weights.dim() == 2 && weights.stride(1) == 1, "Index: weights must be [V, E] with stride [*, 1]");
   RuntimeCheck(destination.dim() == 2 && destination.stride(1) == 1 && destination.size(1) == weights.size(1),
                "Index: destination must be [N, E] with stride [*, 1]");
@@ -145,6 +161,7 @@ void Index(const torch::Tensor &indices, const torch::Tensor &weights, const tor
 void QKNormRopeStoreKV(const torch::Tensor &q, const torch::Tensor &k, const torch::Tensor &v,
                        const torch::Tensor &k_cache, const torch::Tensor &v_cache, const torch::Tensor &indices,
                        const QKNormRope &opts, const torch::Tensor &q_out) {
+  const Range range("yllang::QKNormRopeStoreKV");
   const auto heads_ok = [](const torch::Tensor &t) { return t.dim() == 3 && t.stride(2) == 1 && t.stride(1) == t.size(2); };
   RuntimeCheck(heads_ok(q) && heads_ok(k) && heads_ok(v) && heads_ok(q_out),
                "QKNormRopeStoreKV: q, k, v, q_out must be [N, heads, D] with contiguous heads");
@@ -238,6 +255,7 @@ void DevicePagePool::Reserve(const torch::Tensor &page_table, const torch::Tenso
                              const torch::Tensor &new_len, int page_size,
                              const std::optional<torch::Tensor> &table_index,
                              const std::optional<torch::Tensor> &error_word) {
+  const Range range("yllang::DevicePagePool::Reserve");
   RuntimeCheck(page_table.dim() == 2 && page_table.scalar_type() == torch::kInt32 && page_table.stride(1) == 1 &&
                    page_table.device() == m_device_,
                "DevicePagePool::Reserve: page_table must be int32 [R, W] on the pool's device");
@@ -261,6 +279,7 @@ void DevicePagePool::Reserve(const torch::Tensor &page_table, const torch::Tenso
 void DevicePagePool::Release(const torch::Tensor &page_table, const torch::Tensor &rows,
                              const torch::Tensor &num_tokens, int page_size,
                              const std::optional<torch::Tensor> &error_word) {
+  const Range range("yllang::DevicePagePool::Release");
   RuntimeCheck(page_table.dim() == 2 && page_table.scalar_type() == torch::kInt32 && page_table.stride(1) == 1 &&
                    page_table.device() == m_device_,
                "DevicePagePool::Release: page_table must be int32 [R, W] on the pool's device");
@@ -353,6 +372,7 @@ BatchIndex BuildBatchIndex(const torch::Tensor &prior_len, const torch::Tensor &
                            const std::optional<torch::Tensor> &table_index, int64_t num_pages,
                            int64_t kv_indices_capacity, int64_t slot_capacity, torch::Dtype slot_dtype,
                            const std::optional<torch::Tensor> &error_word) {
+  const Range range("yllang::BuildBatchIndex");
   RuntimeCheck(prior_len.is_cuda(), "BuildBatchIndex: lengths must be CUDA tensors");
   for (const auto *t : {&prior_len, &new_len, &page_table}) {
     RuntimeCheck(t->scalar_type() == torch::kInt32, "BuildBatchIndex: lengths and page table must be int32");
@@ -415,6 +435,7 @@ BatchIndex BuildBatchIndex(const torch::Tensor &prior_len, const torch::Tensor &
 
 // ----------------------------------------------------------------------------
 torch::Tensor Make2DIndices(const torch::Tensor &table, const std::vector<torch::Tensor> &ranges) {
+  const Range range("yllang::Make2DIndices");
   RuntimeCheck(table.dim() == 2, "Make2DIndices: table must be 2-D");
   RuntimeCheck(table.is_cuda(), "Make2DIndices: table must be a CUDA tensor (the indices are made on its device)");
   const int64_t R = static_cast<int64_t>(ranges.size());
@@ -537,6 +558,7 @@ void KVCacheManager::Release(int64_t table_index) {
 }
 
 void KVCacheManager::SyncPageTable() {
+  const Range range("yllang::KVCacheManager::SyncPageTable");
   if (m_dirty_.empty()) return;
   std::sort(m_dirty_.begin(), m_dirty_.end());
   m_dirty_.erase(std::unique(m_dirty_.begin(), m_dirty_.end()), m_dirty_.end());
@@ -560,6 +582,7 @@ void KVCacheManager::SyncPageTable() {
 
 // ----------------------------------------------------------------------------
 Batch BatchManager::NextBatch(const std::vector<RequestSlot> &requests) {
+  const Range range("yllang::BatchManager::NextBatch");
   auto &cache = *m_cache_;
   const int64_t B = static_cast<int64_t>(requests.size());
   int64_t pages = 0, tokens = 0;
