@@ -419,8 +419,9 @@ def run_reference(args, world, rank):
 def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     free, total = torch.cuda.mem_get_info(dev)
-    R, pool_bytes, per_set = plan(args, world, free)
-    batches, desc = make_batches(args.workload, world, pool_bytes, R)
+    shape_world = 1 if args.replicas else world  # replicas: every rank runs the one-GPU shapes
+    R, pool_bytes, per_set = plan(args, shape_world, free)
+    batches, desc = make_batches(args.workload, shape_world, pool_bytes, R)
     b0 = batches[0]
     P = b0.num_pages
     S = P * b0.page_size
@@ -510,7 +511,8 @@ def run_ours(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
         "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded lengths and fragmented page tables, K/V N(0,1) cast to bf16",
-        "config": dict(desc, parallelism=f"kv-head shard x{world}" if world > 1 else "single GPU",
+        "config": dict(desc, parallelism=(f"replicas x{world}" if args.replicas else f"kv-head shard x{world}")
+                       if world > 1 else "single GPU",
                        path=(f"yl_kv_step ({step_mode})" if fused else "build_index + store_kv_cache"),
                        l2=f"inputs rotate over {R} sets ({R * per_set / 1e6:.0f} MB > 2 x L2), "
                           "distinct destination slots per set"),
@@ -528,7 +530,7 @@ def run_ours(args, world, rank, local):
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
                      "traffic": args.traffic if args.traffic is not None else STORE_TRAFFIC_NCU.get(
-                         (args.workload, world)),
+                         (args.workload, shape_world)),
                      "peak_source": f"{peak_kind} hbm_gbs (copy)", "algorithmic_bytes_per_launch": store_bytes,
                      "launch_us": round(store_us, 3),
                      "timing": f"{n_sep} back-to-back launches in one CUDA graph, events around the replays",
@@ -858,6 +860,8 @@ def main():
     ap.add_argument("--no-qkv", action="store_true", help="skip the fused norm/rotary/store line")
     ap.add_argument("--no-pool", action="store_true", help="skip the page-allocator line")
     ap.add_argument("--no-make2d", action="store_true", help="skip the range-expansion (Make2DIndices) line")
+    ap.add_argument("--replicas", action="store_true",
+                    help="every rank runs the full-head one-GPU workload (a sanity check of the head-sharded run)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
