@@ -3,12 +3,14 @@
 // assigns them one libtorch scalar at a time (batch_manager.h:45-47).
 //
 // Every block scans the range lengths itself, 512 ranges at a time, into
-// shared-memory offsets; the output positions of each chunk are striped over
-// the whole grid, and each position finds its range by a binary search over
-// the chunk's offsets.  A range costs 24 bytes of reads per block, an index 8
-// bytes of writes: at the batch sizes NextBatch sees (ranges in the hundreds or
-// thousands, indices in the hundreds of thousands) the kernel is bound by its
-// int64 stores.
+// shared-memory offsets; the output positions of each chunk are cut into
+// tiles of 256, dealt to the grid's warps in turn.  A lane finds the range of
+// its first position by a binary search over the chunk's offsets, then walks
+// forward through its 8 positions (32 apart, so each store instruction of
+// the warp writes 256 contiguous bytes).  A range costs 24 bytes of reads per
+// block, an index 8 bytes of writes: at the batch sizes NextBatch sees
+// (ranges in the hundreds or thousands, indices in the hundreds of thousands)
+// the kernel is bound by its int64 stores.
 #include <cuda_runtime.h>
 
 #include <climits>
@@ -21,6 +23,7 @@ namespace ylk {
 constexpr int kRangeThreads = 512;            // ranges per scan chunk (one per thread)
 constexpr int64_t kRangeLenCap = 1ll << 40;   // longer ranges count as this long
 constexpr int64_t kMaxRanges = 1ll << 22;     // so that sums of capped lengths stay below 2^62
+constexpr int kWarpTile = 32 * 8;             // output positions a warp writes per tile (8 per lane)
 
 struct RangesParams {
   const int64_t *ranges;
@@ -46,7 +49,8 @@ __global__ void __launch_bounds__(kRangeThreads) make_2d_indices_kernel(const __
   __shared__ int64_t warp_base[kRangeThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool report = blockIdx.x == 0;  // every block sees the same ranges: one reports
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kRangeThreads;
+  const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * (kRangeThreads / 32) + warp;
+  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * (kRangeThreads / 32) * kWarpTile;
   int64_t carry = 0;  // indices of the chunks before this one
   for (int c0 = 0; c0 < p.num_ranges; c0 += kRangeThreads) {
     const int n = min(kRangeThreads, p.num_ranges - c0);
@@ -78,14 +82,28 @@ __global__ void __launch_bounds__(kRangeThreads) make_2d_indices_kernel(const __
     __syncthreads();
     const int64_t total = off[n];
     const int64_t limit = min(total, p.capacity - carry);  // <= 0 once the output is full
-    for (int64_t q = static_cast<int64_t>(blockIdx.x) * kRangeThreads + tid; q < limit; q += stride) {
+    int64_t *out = p.indices + carry;
+    for (int64_t t0 = gwarp * kWarpTile; t0 < limit; t0 += warp_stride) {
+      int64_t q = t0 + lane;
+      if (q >= limit) continue;
       // The last range k < n with off[k] <= q: off[k + 1] > q, so range k is
-      // not empty and holds position q.
+      // not empty and holds position q.  Later positions of the lane walk
+      // forward from there (a range change is rare: ranges are long).
       int k = 0;
 #pragma unroll
       for (int step = kRangeThreads / 2; step > 0; step >>= 1)
         if (k + step < n && off[k + step] <= q) k += step;
-      p.indices[carry + q] = first[k] + (q - off[k]);
+      int64_t next = off[k + 1];
+      int64_t base = first[k] - off[k];
+      const int64_t end = min(t0 + kWarpTile, limit);
+      for (; q < end; q += 32) {
+        while (q >= next) {  // ends: q < limit <= off[n]
+          ++k;
+          next = off[k + 1];
+          base = first[k] - off[k];
+        }
+        out[q] = base + q;
+      }
     }
     carry += total;
     __syncthreads();  // off / first / warp_base are rewritten by the next chunk
@@ -125,9 +143,9 @@ extern "C" int yl_make_2d_indices(const yl_ranges_args *a, cudaStream_t stream) 
   p.error_word = a->error_word;
   p.capacity = a->indices_capacity;
   p.num_ranges = static_cast<int32_t>(a->num_ranges);
-  // About four indices per thread over the output; at most two blocks per SM,
-  // each of which rescans every range.
-  const int64_t per_block = 4ll * kRangeThreads;
+  // One tile per warp over the output; at most two blocks per SM, each of
+  // which rescans every range.
+  const int64_t per_block = static_cast<int64_t>(kRangeThreads / 32) * kWarpTile;
   const int64_t want = (a->indices_capacity + per_block - 1) / per_block;
   const int64_t cap = 2ll * sm_count();
   const unsigned grid = static_cast<unsigned>(want < 1 ? 1 : (want < cap ? want : cap));

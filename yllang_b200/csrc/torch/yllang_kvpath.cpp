@@ -455,8 +455,8 @@ torch::Tensor Make2DIndices(const torch::Tensor &table, const std::vector<torch:
     RuntimeCheck(row >= 0 && lo >= 0 && hi >= lo,
                  "Make2DIndices: a range needs row >= 0, col_start >= 0 and col_end >= col_start");
     RuntimeCheck(row <= INT64_MAX - hi, "Make2DIndices: row + col_end passes INT64_MAX");
+    RuntimeCheck(hi - lo < (int64_t{1} << 40) - total, "Make2DIndices: 2^40 indices or more");
     total += hi - lo;
-    RuntimeCheck(total < (int64_t{1} << 40), "Make2DIndices: more than 2^40 indices");
   }
   const auto opts = torch::TensorOptions().dtype(torch::kInt64).device(table.device());
   torch::Tensor out = torch::empty({total}, opts);
