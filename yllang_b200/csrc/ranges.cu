@@ -4,9 +4,9 @@
 //
 // Every block scans the range lengths itself, 512 ranges at a time, into
 // shared-memory offsets; the output positions of each chunk are cut into
-// tiles of 256, dealt to the grid's warps in turn.  A lane finds the range of
+// tiles of 512, dealt to the grid's warps in turn.  A lane finds the range of
 // its first position by a binary search over the chunk's offsets, then walks
-// forward through its 8 positions (32 apart, so each store instruction of
+// forward through its 16 positions (32 apart, so each store instruction of
 // the warp writes 256 contiguous bytes).  A range costs 24 bytes of reads per
 // block, an index 8 bytes of writes: at the batch sizes NextBatch sees
 // (ranges in the hundreds or thousands, indices in the hundreds of thousands)
@@ -23,7 +23,7 @@ namespace ylk {
 constexpr int kRangeThreads = 512;            // ranges per scan chunk (one per thread)
 constexpr int64_t kRangeLenCap = 1ll << 40;   // longer ranges count as this long
 constexpr int64_t kMaxRanges = 1ll << 22;     // so that sums of capped lengths stay below 2^62
-constexpr int kWarpTile = 32 * 8;             // output positions a warp writes per tile (8 per lane)
+constexpr int kWarpTile = 32 * 16;            // output positions a warp writes per tile (16 per lane)
 
 struct RangesParams {
   const int64_t *ranges;
