@@ -368,3 +368,17 @@ def test_missing_library_fails_loudly(tmp_path):
     )
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.startswith("refused:") and "build the CUDA library" in r.stdout
+
+
+def test_python_ops_refuse_host_tensors_and_bad_shapes():
+    """The Python front end's checks run before any launch: host tensors,
+    wrong dtypes and shapes raise PanicError (no CPU path exists)."""
+    import torch
+
+    with pytest.raises(yl.PanicError, match="CUDA"):
+        yl.make_2d_indices(torch.zeros(2, 3, dtype=torch.int64))
+    with pytest.raises(yl.PanicError, match="CUDA"):
+        yl.gather_rows(torch.zeros(3, dtype=torch.int32), torch.zeros(10, 64))
+    with pytest.raises(yl.PanicError, match="CUDA"):
+        yl.store_kv_cache(*(torch.zeros(4, 64) for _ in range(2)), *(torch.zeros(16, 64) for _ in range(2)),
+                          torch.zeros(4, dtype=torch.int64))
