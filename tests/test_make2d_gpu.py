@@ -121,3 +121,26 @@ def test_make2d_drives_next_batch_page_lookup(cuda, path):
     torch.cuda.synchronize()
     assert kv_indices.cpu().tolist() == d["kv_indices"]
     assert slots.cpu().tolist() == d["slot_mapping"]
+
+
+def test_cpp_make2d_range_tensors_and_checks(cuda):
+    """yllang::Make2DIndices takes range tensors of any dtype on the host or
+    the device (the first three entries of each), and refuses what the
+    reference's size_t arithmetic would wrap."""
+    C = yl.load_extension()
+    table = torch.zeros(4, 4, device=cuda)
+    want = [10, 11, 12, 40, 41]
+    for make in (lambda x: torch.tensor(x, dtype=torch.int64, device=cuda),
+                 lambda x: torch.tensor(x, dtype=torch.int32),
+                 lambda x: torch.tensor(x + [99], dtype=torch.float64)):
+        got = C.Make2DIndices(table, [make([10, 0, 3]), make([5, 2, 2]), make([40, 0, 2])])
+        torch.cuda.synchronize()
+        assert got.cpu().tolist() == want
+    assert C.Make2DIndices(table, []).numel() == 0
+    for bad in ([-1, 0, 2], [0, 3, 1], [0, -2, 1]):
+        with pytest.raises(C.PanicError):
+            C.Make2DIndices(table, [torch.tensor(bad)])
+    with pytest.raises(C.PanicError, match="three entries"):
+        C.Make2DIndices(table, [torch.tensor([1, 2])])
+    with pytest.raises(C.PanicError, match="different devices"):
+        C.Make2DIndices(table, [torch.tensor([0, 0, 1]), torch.tensor([0, 0, 1], device=cuda)])
