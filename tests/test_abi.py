@@ -382,3 +382,13 @@ def test_python_ops_refuse_host_tensors_and_bad_shapes():
     with pytest.raises(yl.PanicError, match="CUDA"):
         yl.store_kv_cache(*(torch.zeros(4, 64) for _ in range(2)), *(torch.zeros(16, 64) for _ in range(2)),
                           torch.zeros(4, dtype=torch.int64))
+
+
+def test_device_error_names_and_debug_mode_default_off():
+    C = yl.load_extension()
+    for bits, want in [(0, ""), (0x1, "SLOT_RANGE"), (0x401, "SLOT_RANGE|INDEX_RANGE"),
+                       (0x3000, "POOL_EMPTY|POOL_OVERFLOW"), (0x10002, "PAGE_RANGE|0x10000"), (0x40000, "0x40000")]:
+        assert _abi.deverr_names(bits) == want
+        assert C.DeviceErrorNames(bits) == want
+    if not os.environ.get("YLLANG_CHECK_DEVICE_ERRORS"):
+        assert not yl.ops.CHECK_DEVICE_ERRORS and not C.DeviceErrorChecksEnabled()

@@ -154,6 +154,18 @@ class QkvStoreArgs(ctypes.Structure):
 YL_DTYPE_BF16, YL_DTYPE_F16 = 0, 1
 
 
+def deverr_names(bits: int) -> str:
+    """'SLOT_RANGE|PAGE_RANGE' for a device error word (YL_DEVERR_* bits)."""
+    names = []
+    for name, value in globals().items():
+        if name.startswith("DEVERR_") and bits & value:
+            names.append(name[len("DEVERR_"):])
+            bits &= ~value
+    if bits:
+        names.append(hex(bits))
+    return "|".join(names)
+
+
 class PagePool(ctypes.Structure):
     """struct yl_page_pool."""
 

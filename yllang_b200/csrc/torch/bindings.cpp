@@ -11,6 +11,9 @@ using namespace yllang;
 PYBIND11_MODULE(_C, m) {
   m.doc() = "C++17 libtorch front end of the B200 paged KV store and batch index build";
   py::register_exception<PanicError>(m, "PanicError", PyExc_RuntimeError);
+  m.def("DeviceErrorChecksEnabled", &DeviceErrorChecksEnabled,
+        "true when YLLANG_CHECK_DEVICE_ERRORS was set: calls read their device error bits back and throw");
+  m.def("DeviceErrorNames", &DeviceErrorNames, py::arg("bits"), "names of the YL_DEVERR_* bits in a device error word");
 
   m.def(
       "StoreKVCache",

@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <numeric>
 #include <sstream>
 
@@ -19,6 +20,38 @@ namespace yllang {
 
 void RuntimeCheck(bool cond, const std::string &msg) {
   if (!cond) throw PanicError(msg);
+}
+
+bool DeviceErrorChecksEnabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("YLLANG_CHECK_DEVICE_ERRORS");
+    return e != nullptr && *e != '\0' && std::string(e) != "0";
+  }();
+  return on;
+}
+
+std::string DeviceErrorNames(uint32_t bits) {
+  static const std::pair<uint32_t, const char *> kNames[] = {
+      {YL_DEVERR_SLOT_RANGE, "SLOT_RANGE"},           {YL_DEVERR_PAGE_RANGE, "PAGE_RANGE"},
+      {YL_DEVERR_ROW_OVERFLOW, "ROW_OVERFLOW"},       {YL_DEVERR_INDICES_CAP, "INDICES_CAP"},
+      {YL_DEVERR_SLOTS_CAP, "SLOTS_CAP"},             {YL_DEVERR_NEGATIVE_LEN, "NEGATIVE_LEN"},
+      {YL_DEVERR_INDPTR_OVERFLOW, "INDPTR_OVERFLOW"}, {YL_DEVERR_TABLE_ROW, "TABLE_ROW"},
+      {YL_DEVERR_TOKEN_COUNT, "TOKEN_COUNT"},         {YL_DEVERR_TIMEOUT, "TIMEOUT"},
+      {YL_DEVERR_INDEX_RANGE, "INDEX_RANGE"},         {YL_DEVERR_POSITION_RANGE, "POSITION_RANGE"},
+      {YL_DEVERR_POOL_EMPTY, "POOL_EMPTY"},           {YL_DEVERR_POOL_OVERFLOW, "POOL_OVERFLOW"}};
+  std::string out;
+  for (const auto &[bit, name] : kNames) {
+    if ((bits & bit) == 0) continue;
+    if (!out.empty()) out += '|';
+    out += name;
+    bits &= ~bit;
+  }
+  if (bits != 0) {
+    std::ostringstream os;
+    os << (out.empty() ? "" : "|") << "0x" << std::hex << bits;
+    out += os.str();
+  }
+  return out;
 }
 
 namespace {
@@ -40,6 +73,43 @@ void CheckStatus(int status, const char *what) {
     os << what << ": " << yl_status_string(status) << " (" << status << "): " << yl_last_error();
     throw PanicError(os.str());
   }
+}
+
+// Debug mode (see DeviceErrorChecksEnabled): a call given no device error
+// word runs with a private one; Check() then waits for the stream and throws
+// PanicError naming the bits the kernels raised.
+class DeviceErrorScope {
+ public:
+  DeviceErrorScope(const torch::Device &device, uint32_t *given, const char *what) : m_word_(given), m_what_(what) {
+    if (given == nullptr && DeviceErrorChecksEnabled()) {
+      m_private_ = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).device(device));
+      m_word_ = reinterpret_cast<uint32_t *>(m_private_.data_ptr<int32_t>());
+    }
+  }
+  uint32_t *word() const { return m_word_; }
+  void Check() const {
+    if (!m_private_.defined()) return;
+    const auto bits = static_cast<uint32_t>(m_private_.item<int32_t>());
+    if (bits != 0) {
+      std::ostringstream os;
+      os << m_what_ << ": device error bits 0x" << std::hex << bits << std::dec << " (" << DeviceErrorNames(bits)
+         << ")";
+      throw PanicError(os.str());
+    }
+  }
+
+ private:
+  torch::Tensor m_private_;
+  uint32_t *m_word_;
+  const char *m_what_;
+};
+
+// A caller's device error word: a 4-byte tensor on the call's device.
+uint32_t *ErrorWordOf(const std::optional<torch::Tensor> &w, const torch::Device &device, const char *what) {
+  if (!w) return nullptr;
+  RuntimeCheck(w->numel() >= 1 && w->element_size() == 4 && w->device() == device,
+               std::string(what) + ": error_word must be a 4-byte tensor on the call's CUDA device");
+  return static_cast<uint32_t *>(w->data_ptr());
 }
 
 cudaStream_t CurrentStream(const torch::Tensor &t) {
@@ -82,9 +152,11 @@ void LaunchStore(const torch::Tensor &k, const torch::Tensor &v, const torch::Te
     a.cache_layer_stride = k_cache.stride(0) * item;
   }
   a.num_slots = num_slots;
-  a.error_word = error_word;
+  const DeviceErrorScope errors(k.device(), error_word, "yl_kv_store");
+  a.error_word = errors.word();
   const c10::cuda::CUDAGuard guard(k.device());
   CheckStatus(yl_kv_store(&a, CurrentStream(k)), "yl_kv_store");
+  errors.Check();
 }
 
 void CheckIndices(const torch::Tensor &indices, int64_t n, const torch::Tensor &k) {
@@ -154,8 +226,11 @@ void Index(const torch::Tensor &indices, const torch::Tensor &weights, const tor
   a.table_row_stride = weights.stride(0) * item;
   a.out_row_stride = destination.stride(0) * item;
   a.num_rows = weights.size(0);
+  const DeviceErrorScope errors(weights.device(), nullptr, "yl_gather_rows");
+  a.error_word = errors.word();
   const c10::cuda::CUDAGuard guard(weights.device());
   CheckStatus(yl_gather_rows(&a, CurrentStream(weights)), "yl_gather_rows");
+  errors.Check();
 }
 
 void QKNormRopeStoreKV(const torch::Tensor &q, const torch::Tensor &k, const torch::Tensor &v,
@@ -229,8 +304,11 @@ void QKNormRopeStoreKV(const torch::Tensor &q, const torch::Tensor &k, const tor
   a.q_out_row_stride = q_out.stride(0) * item;
   a.cache_row_stride = k_cache.stride(0) * item;
   a.num_slots = k_cache.size(0);
+  const DeviceErrorScope errors(q.device(), nullptr, "yl_qkv_norm_rope_store");
+  a.error_word = errors.word();
   const c10::cuda::CUDAGuard guard(q.device());
   CheckStatus(yl_qkv_norm_rope_store(&a, CurrentStream(q)), "yl_qkv_norm_rope_store");
+  errors.Check();
 }
 
 // ----------------------------------------------------------------------------
@@ -271,9 +349,12 @@ void DevicePagePool::Reserve(const torch::Tensor &page_table, const torch::Tenso
   a.max_pages_per_row = static_cast<int32_t>(page_table.size(1));
   a.page_size = page_size;
   a.batch_size = static_cast<int32_t>(B);
-  a.error_word = error_word ? reinterpret_cast<uint32_t *>(error_word->data_ptr()) : nullptr;
+  const DeviceErrorScope errors(m_device_, ErrorWordOf(error_word, m_device_, "DevicePagePool::Reserve"),
+                                "yl_reserve_pages");
+  a.error_word = errors.word();
   const c10::cuda::CUDAGuard guard(m_device_);
   CheckStatus(yl_reserve_pages(&a, c10::cuda::getCurrentCUDAStream(m_device_.index()).stream()), "yl_reserve_pages");
+  errors.Check();
 }
 
 void DevicePagePool::Release(const torch::Tensor &page_table, const torch::Tensor &rows,
@@ -294,9 +375,12 @@ void DevicePagePool::Release(const torch::Tensor &page_table, const torch::Tenso
   a.max_pages_per_row = static_cast<int32_t>(page_table.size(1));
   a.page_size = page_size;
   a.num_release = static_cast<int32_t>(R);
-  a.error_word = error_word ? reinterpret_cast<uint32_t *>(error_word->data_ptr()) : nullptr;
+  const DeviceErrorScope errors(m_device_, ErrorWordOf(error_word, m_device_, "DevicePagePool::Release"),
+                                "yl_release_pages");
+  a.error_word = errors.word();
   const c10::cuda::CUDAGuard guard(m_device_);
   CheckStatus(yl_release_pages(&a, c10::cuda::getCurrentCUDAStream(m_device_.index()).stream()), "yl_release_pages");
+  errors.Check();
 }
 
 int64_t DevicePagePool::FreeCount() const { return m_free_count_.item<int32_t>(); }
@@ -423,13 +507,12 @@ BatchIndex BuildBatchIndex(const torch::Tensor &prior_len, const torch::Tensor &
   a.slot_mapping = slot_capacity ? out.slot_mapping.data_ptr() : nullptr;
   a.kv_indices_capacity = kv_indices_capacity;
   a.slot_capacity = slot_capacity;
-  if (error_word) {
-    RuntimeCheck(error_word->numel() >= 1 && error_word->element_size() == 4 && error_word->is_cuda(),
-                 "BuildBatchIndex: error_word must be a 4-byte CUDA tensor");
-    a.error_word = static_cast<uint32_t *>(error_word->data_ptr());
-  }
+  const DeviceErrorScope errors(prior_len.device(), ErrorWordOf(error_word, prior_len.device(), "BuildBatchIndex"),
+                                "yl_build_index");
+  a.error_word = errors.word();
   const c10::cuda::CUDAGuard guard(prior_len.device());
   CheckStatus(yl_build_index(&a, CurrentStream(prior_len)), "yl_build_index");
+  errors.Check();
   return out;
 }
 

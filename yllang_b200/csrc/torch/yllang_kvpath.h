@@ -32,6 +32,17 @@ class PanicError final : public std::runtime_error {
 // Throws PanicError(msg) when cond is false.
 void RuntimeCheck(bool cond, const std::string &msg);
 
+// Debug mode, off by default: YLLANG_CHECK_DEVICE_ERRORS=1 in the environment
+// (read once per process).  Every front-end call that is given no device
+// error word then runs its kernels with a private one, waits for the stream
+// and throws PanicError naming the bits they raised (a slot or page id out of
+// range, a short page-table row, a full pool, ...) — the host-side check of
+// what the kernels otherwise skip and only flag.  It makes every call
+// synchronous.
+bool DeviceErrorChecksEnabled();
+// "SLOT_RANGE|PAGE_RANGE" for a device error word (YL_DEVERR_* bits).
+std::string DeviceErrorNames(uint32_t bits);
+
 // ----------------------------------------------------------------------------
 // Store
 // ----------------------------------------------------------------------------

@@ -10,6 +10,7 @@ launch, as RuntimeCheck does in the reference (src/include/util/panic.h:35).
 """
 from __future__ import annotations
 
+import os
 from typing import NamedTuple
 
 import torch
@@ -24,6 +25,42 @@ class PanicError(RuntimeError):
 def _check(cond: bool, msg: str) -> None:
     if not cond:
         raise PanicError(msg)
+
+
+# Debug mode, off by default: YLLANG_CHECK_DEVICE_ERRORS=1 in the environment
+# (read at import).  A call given no device error word then runs its kernels
+# with a private one, waits for it and raises PanicError naming the bits they
+# raised (the check of what the kernels otherwise skip and only flag).  Every
+# such call becomes synchronous, so it cannot be captured in a CUDA graph.
+CHECK_DEVICE_ERRORS = os.environ.get("YLLANG_CHECK_DEVICE_ERRORS", "") not in ("", "0")
+
+
+def _word(error_word: torch.Tensor | None, device: torch.device, what: str) -> int | None:
+    """Device pointer of a caller's error word: a 4-byte tensor on `device`."""
+    if error_word is None:
+        return None
+    _check(error_word.is_cuda and error_word.device == device and error_word.element_size() == 4
+           and error_word.numel() >= 1, f"{what}: error_word must be a 4-byte tensor on {device}")
+    return error_word.data_ptr()
+
+
+class _Errors:
+    """The error word of one call: the caller's, or in debug mode a private
+    one that check() reads back after the launch."""
+
+    def __init__(self, error_word: torch.Tensor | None, device: torch.device, what: str):
+        self.what = what
+        self.private = None
+        self.tensor = error_word
+        if error_word is None and CHECK_DEVICE_ERRORS:
+            self.private = self.tensor = torch.zeros(1, dtype=torch.int32, device=device)
+        self.ptr = _word(self.tensor, device, what)
+
+    def check(self) -> None:
+        if self.private is not None:
+            bits = int(self.private.item()) & 0xFFFFFFFF
+            if bits:
+                raise PanicError(f"{self.what}: device error bits {bits:#x} ({_abi.deverr_names(bits)})")
 
 
 def _stream(stream: torch.cuda.Stream | None, device: torch.device) -> int:
@@ -77,7 +114,7 @@ def store_args(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache:
         a.v_layer_stride = v.stride(0) * item
         a.cache_layer_stride = k_cache.stride(0) * item
     a.num_slots = k_cache.shape[-2] if check_slots else 0
-    a.error_word = error_word.data_ptr() if error_word is not None else None
+    a.error_word = _word(error_word, k.device, "store")
     return a
 
 
@@ -92,8 +129,10 @@ def store_kv_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_ca
     """
     if k.shape[-2] == 0:
         return
-    args = store_args(k, v, k_cache, v_cache, slots, error_word)
+    errs = _Errors(error_word, k.device, "store_kv_cache")
+    args = store_args(k, v, k_cache, v_cache, slots, errs.tensor)
     _abi.check(_abi.kv_store_raw(args, _stream(stream, k.device)))
+    errs.check()
 
 
 class BatchIndex(NamedTuple):
@@ -162,8 +201,10 @@ def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torc
                          torch.empty(B, **i32), torch.empty(B + 1, **i32),
                          torch.empty(slot_capacity, dtype=slot_dtype, device=dev))
     _check_out(out, B, dev)
-    a = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, error_word)
+    errs = _Errors(error_word, dev, "build_index")
+    a = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, errs.tensor)
     _abi.check(_abi.build_index_raw(a, _stream(stream, dev)))
+    errs.check()
     return out
 
 
@@ -186,7 +227,7 @@ def index_args(prior_len, new_len, page_table, page_size, table_index, num_pages
     a.slot_mapping = out.slot_mapping.data_ptr()
     a.kv_indices_capacity = out.kv_indices.numel()
     a.slot_capacity = out.slot_mapping.numel()
-    a.error_word = error_word.data_ptr() if error_word is not None else None
+    a.error_word = _word(error_word, prior_len.device, "index")
     return a
 
 
@@ -209,8 +250,10 @@ def kv_step(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torch.Te
     _check(out.slot_mapping.numel() >= N, f"out.slot_mapping holds {out.slot_mapping.numel()} < N={N} slots")
     a = _abi.StepArgs()
     a.store = store_args(k, v, k_cache, v_cache, out.slot_mapping[:N], None)
-    a.index = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, error_word)
+    errs = _Errors(error_word, prior_len.device, "kv_step")  # the step reports store errors here too
+    a.index = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, errs.tensor)
     _abi.check(_abi.kv_step_raw(a, _stream(stream, k.device)))
+    errs.check()
     return out
 
 
@@ -241,8 +284,10 @@ def gather_rows(indices: torch.Tensor, table: torch.Tensor, out: torch.Tensor | 
     a.table_row_stride = table.stride(0) * item
     a.out_row_stride = out.stride(0) * item
     a.num_rows = table.shape[0]
-    a.error_word = error_word.data_ptr() if error_word is not None else None
+    errs = _Errors(error_word, table.device, "gather_rows")
+    a.error_word = errs.ptr
     _abi.check(_abi.gather_rows_raw(a, _stream(stream, table.device)))
+    errs.check()
     return out
 
 
@@ -285,8 +330,10 @@ def make_2d_indices(ranges: torch.Tensor, out: torch.Tensor | None = None, count
     a.count = count.data_ptr() if count is not None else None
     a.num_ranges = ranges.shape[0]
     a.indices_capacity = out.numel()
-    a.error_word = error_word.data_ptr() if error_word is not None else None
+    errs = _Errors(error_word, dev, "make_2d_indices")
+    a.error_word = errs.ptr
     _abi.check(_abi.make_2d_indices_raw(a, _stream(stream, dev)))
+    errs.check()
     return out
 
 
@@ -371,8 +418,10 @@ def qkv_norm_rope_store(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cac
     a.q_out_row_stride = q_out.stride(0) * item
     a.cache_row_stride = k_cache.stride(0) * item
     a.num_slots = k_cache.shape[0]
-    a.error_word = error_word.data_ptr() if error_word is not None else None
+    errs = _Errors(error_word, q.device, "qkv_norm_rope_store")
+    a.error_word = errs.ptr
     _abi.check(_abi.qkv_store_raw(a, _stream(stream, q.device)))
+    errs.check()
     return q_out
 
 
@@ -421,8 +470,10 @@ class DevicePagePool:
         a.new_len = self._vec(new_len, B, "new_len")
         a.table_index = self._vec(table_index, B, "table_index") if table_index is not None else None
         a.page_size, a.batch_size = page_size, B
-        a.error_word = error_word.data_ptr() if error_word is not None else None
+        errs = _Errors(error_word, self.device, "DevicePagePool.reserve")
+        a.error_word = errs.ptr
         _abi.check(_abi.reserve_pages_raw(a, _stream(stream, self.device)))
+        errs.check()
 
     def release(self, page_table: torch.Tensor, rows: torch.Tensor, num_tokens: torch.Tensor, page_size: int,
                 error_word: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
@@ -435,8 +486,10 @@ class DevicePagePool:
         a.rows = self._vec(rows, R, "rows")
         a.num_tokens = self._vec(num_tokens, R, "num_tokens")
         a.page_size, a.num_release = page_size, R
-        a.error_word = error_word.data_ptr() if error_word is not None else None
+        errs = _Errors(error_word, self.device, "DevicePagePool.release")
+        a.error_word = errs.ptr
         _abi.check(_abi.release_pages_raw(a, _stream(stream, self.device)))
+        errs.check()
 
     def free_count(self) -> int:
         return int(self.count.item())
