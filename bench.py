@@ -15,17 +15,27 @@ replicated on each rank.  `value` = store bytes moved by all ranks per step
 (algorithmic: read + write of every K and V row, plus the slots) / the step
 time, max over ranks.
 
-Inputs rotate over R sets of K/V rows and page tables (R * per-step inputs >
-2 x the 126 MB L2, distinct destination slots per set), so neither the reads
-nor the scattered writes are absorbed by L2 between steps.  The timed steps
-run as CUDA-graph replays (the way a serving engine launches a decode step);
-events recorded inside the graphs time every index and store launch.
+Before timing, the first warm-up step of every workload is verified on the
+device: all five index arrays against their definition (computed here with
+torch ops from the lengths and page table), every written pool row against its
+input row, and a seeded sample of sentinel-filled pool rows outside the step's
+slots unchanged.  Inputs rotate over R sets of K/V rows and page tables
+(R * per-step inputs > 2 x the 126 MB L2, distinct destination slots per set),
+so neither the reads nor the scattered writes are absorbed by L2 between
+steps.  The timed steps run as CUDA-graph replays (the way a serving engine
+launches a decode step), queued behind a bounded device-side delay so that the
+events around them time the kernels, not the host's graph launch.
+
+The default line also carries, as sub-objects, the other workloads (ragged
+prefill, Qwen2-72B decode split over the ranks' KV heads, mixed batches), each
+verified the same way, and the (f)-row kernels.
 
   python bench.py [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 """
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -46,11 +56,18 @@ from yllang_b200 import sharding, workloads  # noqa: E402
 METRIC = "KV-store GB/s (% of HBM peak) + tokens/s stored; index-build µs/batch"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one all-layer store launch of the single-GPU
-# Llama-3-8B decode step, from one ncu capture of store_rows_kernel at that
-# launch shape: 33,565,440 read + 1,564,928 written (the rows' writes stay in
-# L2 during the launch and are written back after it).
-STORE_TRAFFIC_NCU = {("llama3_decode", 1): 35130368}
+# DRAM bytes (read + write) per step of the timed step's kernels, from one ncu
+# capture of three consecutive steps with caches left warm between them (so
+# each launch's DRAM writes include the write-back of the lines the previous
+# launch left dirty in L2); keyed by (workload, ranks).
+STEP_TRAFFIC_NCU: dict = {}
+# Device-side delay queued ahead of each timed region (seconds at the maximum
+# SM clock): the host enqueues the graphs while the GPU spins, so the start
+# event is taken with the timed work already queued.
+LEAD_SECONDS = 2e-3
+# Workloads measured as sub-objects of the default line (config names of the
+# workload generator); --extras overrides.
+DEFAULT_EXTRAS = ("ragged_prefill", "qwen72b_decode", "mixed_ps1_hd64", "mixed_ps16_hd128", "mixed_ps64_hd256")
 
 
 # ---------------------------------------------------------------------------
@@ -180,7 +197,7 @@ def make_batches(name: str, world: int, pool_bytes: int, rotate: int):
     for b in batches:
         b.kv_heads = heads
     desc.update(layers=layers, kv_heads_per_gpu=heads, head_dim=batches[0].head_dim, page_size=ps,
-                pool_pages_per_gpu=P, pool_gb_per_gpu=round(2 * layers * P * ps * row / 1e9, 1))
+                pool_pages_per_gpu=P, pool_gb_per_gpu=round(2 * layers * P * ps * batches[0].row_bytes / 1e9, 1))
     return batches, desc
 
 
@@ -221,15 +238,21 @@ def input_bytes(b: workloads.Batch) -> int:
     return 2 * b.layers * b.tokens * b.row_bytes + b.page_table.nbytes
 
 
-def plan(args, world, free_bytes):
+def plan(args, world, free_bytes, workload=None):
     """Pick the rotation count (inputs over 2.2 x L2 unless one set already is)
     and the pool size (what is left after the inputs, at most --pool-gb)."""
-    probe, _ = make_batches(args.workload, world, 150e9, 1)  # lengths only; any pool that fits the step
+    probe, _ = make_batches(workload or args.workload, world, 150e9, 1)  # lengths only
     per_set = input_bytes(probe[0])
     R = args.rotate if args.rotate > 0 else max(1, min(8, math.ceil(2.2 * L2_BYTES / per_set)))
     pool_bytes = min(args.pool_gb * 1e9, free_bytes - R * per_set - 12e9)
     assert pool_bytes > 0, "not enough device memory for the inputs"
     return R, pool_bytes, per_set
+
+
+def device_lead():
+    """Queue a bounded device-side delay (torch's clock64 spin kernel, which
+    ends on its own after the given cycles) ahead of a timed region."""
+    torch.cuda._sleep(int(LEAD_SECONDS * 1.965e9))
 
 
 def capture(order, launches):
@@ -246,9 +269,11 @@ def capture(order, launches):
 
 def time_graphs(graphs, reps=1):
     """Device time (ms) of replaying `graphs` in order, `reps` times, bracketed
-    by events on the launching stream after a synchronize."""
+    by events on the launching stream after a synchronize and a device delay
+    that keeps the host's graph launch out of the interval."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    device_lead()
     start.record()
     for _ in range(reps):
         for g in graphs:
@@ -276,36 +301,288 @@ def load_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-# ---------------------------------------------------------------------------
-# CPU baseline (oracle port, all host threads), bounded sample
-# ---------------------------------------------------------------------------
-def cpu_store_step_sample(b: workloads.Batch, seconds: float, threads: int | None = None):
-    """Time the oracle's index build + store of this batch on the host cores
-    for about `seconds`, the pool scaled to 4 GB of host memory and the inputs
-    rotating over sets larger than the last-level cache."""
-    from oracle import kvpath as orc
+class Workload:
+    """One workload on this rank: R rotation sets of device inputs and
+    outputs, the all-layer pool [2, L, pages * page_size, H_l * D] and the
+    step's launches."""
 
-    threads = threads or orc.max_threads()
-    sets, pool = host_step_setup(b)
-    for hb, k, v in sets:  # first touch of the pool pages and of every input set
-        host_step(hb, pool, k, v, threads)
+    def __init__(self, name: str, args, shape_world: int, dev, rank: int):
+        free, _ = torch.cuda.mem_get_info(dev)
+        self.name = name
+        self.R, pool_bytes, self.per_set = plan(args, shape_world, free, name)
+        self.batches, self.desc = make_batches(name, shape_world, pool_bytes, self.R)
+        b0 = self.batches[0]
+        self.b0 = b0
+        S = b0.num_pages * b0.page_size
+        self.pool = torch.empty((2, b0.layers, S, b0.kv_heads * b0.head_dim), dtype=torch.bfloat16, device=dev)
+        self.k_pool, self.v_pool = self.pool[0], self.pool[1]
+        self.steps = [Step(b, dev, seed=1000 * rank + r) for r, b in enumerate(self.batches)]
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.fused = args.path == "fused"
+
+    def launches(self, r):
+        s, e = self.steps[r], self.err
+        if self.fused:
+            return [lambda: s.fused(self.k_pool, self.v_pool, e)]
+        return [lambda: s.index(e), lambda: s.store(self.k_pool, self.v_pool, e)]
+
+    def check_err(self, when: str):
+        torch.cuda.synchronize()
+        bits = int(self.err.item())
+        assert bits == 0, f"{self.name}: device error word {bits:#x} ({yl._abi.deverr_names(bits)}) {when}"
+
+    def release(self):
+        for n in ("pool", "k_pool", "v_pool", "steps", "batches"):
+            setattr(self, n, None)
+        gc.collect()
+        torch.cuda.empty_cache()
+
+
+def expected_index(s: Step) -> dict:
+    """The five index arrays of a step by their definition, computed on the
+    device with torch ops from the step's lengths and page table: page counts
+    ceil((prior + new) / page_size) and their running sums, each sequence's
+    first pages, its last page's fill, and the slot page * page_size + offset
+    of each new token's position."""
+    ps = s.b.page_size
+    prior, new = s.prior.long().clamp(min=0), s.new.long().clamp(min=0)
+    total = prior + new
+    W = s.table.shape[1]
+    pages = torch.clamp((total + ps - 1) // ps, max=W)
+    zero = torch.zeros(1, dtype=torch.int64, device=prior.device)
+    qo = torch.cat([zero, new.cumsum(0)])
+    seq = torch.repeat_interleave(torch.arange(prior.shape[0], device=prior.device), new)
+    pos = prior[seq] + torch.arange(seq.shape[0], device=prior.device) - qo[seq]
+    return {"kv_indptr": torch.cat([zero, pages.cumsum(0)]),
+            "kv_indices": s.table[torch.arange(W, device=prior.device)[None, :] < pages[:, None]],
+            "kv_last_page_len": torch.where(pages == 0, 0, (total - 1) % ps + 1),
+            "qo_indptr": qo,
+            "slot_mapping": s.table[seq, pos // ps].long() * ps + pos % ps}
+
+
+def verify_first_step(wl: Workload, sample_rows: int = 1 << 16, seed: int = 17) -> dict:
+    """Run the workload's first step once through the timed path and check it
+    on the device: every index array element, every pool row the step wrote
+    (K and V of every layer) against its input row, and `sample_rows` pool
+    rows outside the step's slots -- set to random sentinel values first --
+    unchanged.  Raises AssertionError on any difference."""
+    s = wl.steps[0]
+    b = s.b
+    dev = s.k.device
+    L, S, E = wl.k_pool.shape
+    want = expected_index(s)
+    written = want["slot_mapping"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    flat = wl.pool.view(2 * L * S, E)
+    cand = torch.randint(0, 2 * L * S, (sample_rows,), generator=g, device=dev)
+    cand = cand[~torch.isin(cand % S, written)]
+    sentinel = torch.randn(cand.shape[0], E, generator=g, device=dev).to(torch.bfloat16)
+    flat[cand] = sentinel
+    before = flat[cand].clone()  # repeated candidates keep the last sentinel written
+    for fn in wl.launches(0):
+        fn()
+    wl.check_err("on the verified step")
+    for name, w in want.items():
+        got = getattr(s.out, name)
+        assert torch.equal(got[:w.shape[0]].long(), w.long()), f"{wl.name}: {name} differs from its definition"
+    for layer in range(L):
+        assert torch.equal(wl.k_pool[layer].index_select(0, written), s.k[layer]), f"{wl.name}: K rows, layer {layer}"
+        assert torch.equal(wl.v_pool[layer].index_select(0, written), s.v[layer]), f"{wl.name}: V rows, layer {layer}"
+    assert torch.equal(flat[cand], before), f"{wl.name}: a pool row outside the step's slots changed"
+    n_idx = sum(int(w.numel()) for w in want.values())
+    return {"index_elements": n_idx, "pool_rows": 2 * L * b.tokens, "sentinel_rows": int(cand.shape[0]),
+            "result": "bit-exact"}
+
+
+def time_steps(wl: Workload, K: int, chunk: int, clocks=None) -> float:
+    """Device time (ms) of K steps on this rank: graphs of `chunk` steps
+    (rotation sets in turn) replayed back to back after a device delay."""
+    C = min(K, chunk)
+    q, rem = divmod(K, C)
+    g_main = capture([j % wl.R for j in range(C)], wl.launches)
+    g_rem = capture([(q * C + j) % wl.R for j in range(rem)], wl.launches) if rem else None
+    g_main.replay()  # untimed graph warm-up
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    region = clocks if clocks is not None else _NoClocks()
+    with region:
+        device_lead()
+        start.record()
+        for _ in range(q):
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    del g_main, g_rem
+    return ms
+
+
+class _NoClocks:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def launches_per_step(wl: Workload) -> int:
+    """Kernels of this project one timed step launches (see yl_kv_step)."""
+    b = wl.b0
+    index_launches = 2 if b.batch > 16384 else 1
+    mode = os.environ.get("YL_STEP_MODE", "pdl")
+    if not wl.fused:
+        return index_launches + 1
+    if mode == "fused" and b.batch <= 4096:
+        return 1
+    return index_launches + 1
+
+
+def measure(wl: Workload, args, world: int, steps: int, warmup: int, clocks=None) -> dict:
+    """Verify, warm up and time one workload on every rank (same collectives
+    in the same order on every rank); returns this rank's view of the
+    numbers, times as the max over ranks."""
+    check = verify_first_step(wl)
+    for w in range(1, warmup):
+        for fn in wl.launches(w % wl.R):
+            fn()
+    wl.check_err("during warm-up")
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = time_steps(wl, steps, args.chunk, clocks)
+    barrier(world)
+    wl.check_err("in the timed steps")
+    per_rank = [x / steps * 1e3 for x in sharding.gather_over_ranks(ms)] if world > 1 else [ms / steps * 1e3]
+    step_us = max(per_rank)
+    n_sep = min(max(steps, 8), 256)
+    index_us = reduce_max(per_launch_us(wl.R, lambda r: [lambda: wl.steps[r].index(wl.err)], n_sep), world)
+    store_us = reduce_max(per_launch_us(wl.R, lambda r: [lambda: wl.steps[r].store(wl.k_pool, wl.v_pool, wl.err)],
+                                        n_sep), world)
+    wl.check_err("in the kernel timings")
+    b = wl.b0
+    return {"verified": check, "step_us": step_us, "per_rank_step_us": per_rank, "index_us": index_us,
+            "store_us": store_us, "store_bytes": b.store_bytes(), "step_bytes": b.step_bytes(),
+            "index_bytes": b.index_bytes(), "tokens": b.tokens, "launches_per_step": launches_per_step(wl)}
+
+
+def rank_stats(per_rank: list[float]) -> dict:
+    return {"min": round(min(per_rank), 3), "median": round(statistics.median(per_rank), 3),
+            "max": round(max(per_rank), 3), "all": [round(x, 3) for x in per_rank]}
+
+
+def summarize(m: dict, desc: dict, world: int, peak: float) -> dict:
+    """Numbers of one measured workload: whole-job GB/s and tokens/s, and the
+    roofline of the timed step on one rank (its algorithmic bytes over its
+    time, against the measured copy peak)."""
+    per_s = m["step_us"] * 1e-6
+    step_gbs = m["step_bytes"] / per_s / 1e9
+    out = {"workload": desc["workload"], "scaling": desc["scaling"], "global_batch": desc["global_batch"],
+           "layers": desc["layers"], "kv_heads_per_gpu": desc["kv_heads_per_gpu"], "head_dim": desc["head_dim"],
+           "page_size": desc["page_size"], "tokens_per_step": m["tokens"],
+           "step_us": round(m["step_us"], 3),
+           "value_gbs": round(m["store_bytes"] * world / per_s / 1e9, 1),
+           "tokens_per_s": round(m["tokens"] / per_s, 1),
+           "step_gbs_per_gpu": round(step_gbs, 1), "frac_of_measured_hbm": round(step_gbs / peak, 4),
+           "index_build_us": round(m["index_us"], 3), "store_us": round(m["store_us"], 3),
+           "store_frac_of_measured_hbm": round(m["store_bytes"] / (m["store_us"] * 1e-6) / 1e9 / peak, 4),
+           "verified": m["verified"]}
+    if world > 1:
+        out["per_rank_step_us"] = rank_stats(m["per_rank_step_us"])
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's path as libtorch CPU ops on the host cores
+# ---------------------------------------------------------------------------
+HOST_ROTATE_BYTES = 600e6  # host input sets cycled through: more than a server's last-level cache
+
+
+def host_step_setup(b: workloads.Batch, pool_gb: float = 4.0):
+    """Host copies of the batch for the CPU arms: the pool scaled down to
+    pool_gb (same row and page size; read-only pages alias, written pages
+    stay unique) and enough input sets -- K/V rows as raw bf16 bits, page
+    tables with their own page ids -- that one pass over them (> 600 MB) does
+    not fit a CPU's last-level cache, as the GPU arm rotates past its L2."""
+    P = max(workloads.pool_pages_for(pool_gb * 1e9, b.layers, b.row_bytes, b.page_size), b.tokens + 1)
+    per_set = 2 * b.layers * b.tokens * b.row_bytes
+    R = max(1, min(16, int(math.ceil(HOST_ROTATE_BYTES / per_set))))
+    sets = []
+    for r in range(R):
+        if b.name == "llama3_decode":
+            hb = workloads.llama3_decode(P, batch=b.batch, kv_heads=b.kv_heads, layers=b.layers, seed_pages=2 + r)
+        elif b.name == "ragged_prefill":
+            hb = workloads.ragged_prefill(P, requests=b.batch, kv_heads=b.kv_heads, layers=b.layers,
+                                          seed_pages=2 + r)
+        else:
+            hb = b
+        E = hb.kv_heads * hb.head_dim
+        rng = np.random.default_rng(r)
+        n = hb.layers * hb.tokens * E
+        k = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
+        v = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
+        sets.append((hb, k, v))
+    hb = sets[0][0]
+    pool = np.zeros((2, hb.layers, hb.num_pages * hb.page_size, hb.kv_heads * hb.head_dim), np.uint16)
+    return sets, pool
+
+
+def c_port_step(hb, pool, k, v, threads):
+    from oracle import kvpath as orc
+    out = orc.build_index(hb.prior_len, hb.new_len, hb.page_table, hb.page_size, num_pages=hb.num_pages)
+    orc.store(k, v, pool[0], pool[1], out["slot_mapping"], num_slots=pool.shape[2], threads=threads)
+
+
+class TorchHost:
+    """The step as libtorch CPU ops (the reference's host code runs its tensor
+    work through libtorch): the index arrays by vectorised torch ops and the
+    store as index_copy_ of each layer's K and V rows into the [pages *
+    page_size, row] pool views, on torch's intra-op threads."""
+
+    def __init__(self, sets, pool):
+        as_t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).view(torch.int16)
+        self.sets = [(hb, torch.from_numpy(hb.prior_len), torch.from_numpy(hb.new_len),
+                      torch.from_numpy(hb.page_table), as_t(k), as_t(v)) for hb, k, v in sets]
+        self.pool = torch.from_numpy(pool).view(torch.int16)
+
+    def step(self, r: int):
+        from oracle import kvpath as orc
+        hb, prior, new, table, k, v = self.sets[r % len(self.sets)]
+        idx = orc.torch_build_index(prior, new, table, hb.page_size)
+        orc.torch_store(k, v, self.pool[0], self.pool[1], idx["slot_mapping"])
+
+
+def timed_host_steps(fn, seconds: float, min_reps: int = 3):
+    """Run fn(rep) (after one untimed pass over every set) for about `seconds`;
+    returns (seconds per step, steps run)."""
     reps, t0 = 0, time.perf_counter()
     while True:
-        hb, k, v = sets[reps % len(sets)]
-        host_step(hb, pool, k, v, threads)
+        fn(reps)
         reps += 1
         el = time.perf_counter() - t0
-        if el >= seconds and reps >= 3:
-            break
-    per_step = el / reps
+        if el >= seconds and reps >= min_reps:
+            return el / reps, reps
+
+
+def cpu_store_step_sample(b: workloads.Batch, seconds: float) -> dict:
+    """cpu_baseline of the default line: the libtorch CPU step on all host
+    threads for about `seconds`, the pool scaled to 4 GB of host memory and
+    the inputs rotating past the last-level cache."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    sets, pool = host_step_setup(b)
+    th = TorchHost(sets, pool)
+    for r in range(len(sets)):
+        th.step(r)
+    per_step, reps = timed_host_steps(th.step, seconds)
     hb = sets[0][0]
     gbs = hb.store_bytes() / per_step / 1e9
-    return {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+    return {"value": round(gbs, 2), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{reps} full steps of {hb.name} (B={hb.batch}, N={hb.tokens}, L={hb.layers}, "
-                      f"row {hb.row_bytes} B) into a {pool.nbytes / 1e9:.1f} GB host pool, index build + store, "
-                      f"C oracle on {threads} threads, inputs rotating over {len(sets)} sets "
+                      f"row {hb.row_bytes} B) into a {pool.nbytes / 1e9:.1f} GB host pool: index arrays by "
+                      f"libtorch CPU ops, store by index_copy_ per layer, {torch.get_num_threads()} intra-op threads, "
+                      f"inputs rotating over {len(sets)} sets "
                       f"({len(sets) * 2 * hb.layers * hb.tokens * hb.row_bytes / 1e6:.0f} MB)",
-            "ms_per_step": round(per_step * 1e3, 3)}
+            "ms_per_step": round(per_step * 1e3, 3), "hardware_concurrency": os.cpu_count()}
 
 
 def ref_make2d_us(b: workloads.Batch, max_seconds: float = 5.0):
@@ -336,62 +613,87 @@ def ref_make2d_us(b: workloads.Batch, max_seconds: float = 5.0):
             "note": "reference Make2DIndices, one libtorch scalar op per element, scaled from the sample"}
 
 
+def ref_gpu_store(args, b: workloads.Batch, peak: float) -> dict | None:
+    """The reference's own store kernel (StoreKVCacheKernel through its
+    StoreKVCache launcher, src/kvcache/store_kv_cache.cu:46-163, built from the
+    reference sources for sm_100a in oracle/_ref) on this box's GPU, launched
+    as the reference launches it: one call per layer (MHAKVCache::StoreKV,
+    src/include/kvcache/mha_kvcache.h:76-86), int64 slots, the same batch,
+    pool and input rotation as the GPU arm.  The slots come from our index
+    build (the reference builds them on the host)."""
+    import ctypes
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_store.so")
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    if not os.path.exists(path):
+        return {"unavailable": "reference store harness not built (make -C oracle ref)"}
+    f = ctypes.CDLL(path).ref_store_kv_cache
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int] + [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 4
+    if b.row_bytes not in (512, 1024, 2048, 4096):
+        return {"unavailable": f"the reference's Copy<> has no {b.row_bytes}-byte rows"}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = Workload(args.workload, args, 1, dev, 0)
+    try:
+        for s in wl.steps:
+            s.index(wl.err)
+        wl.check_err("building the slots for the reference store")
+        L = wl.b0.layers
+
+        def layer_calls(r):
+            s = wl.steps[r]
+
+            def call(layer):
+                def go():
+                    k, v = s.k[layer], s.v[layer]
+                    kc, vc = wl.k_pool[layer], wl.v_pool[layer]
+                    rc = f(k.shape[1] * 2, 0, 0, k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                           s.out.slot_mapping.data_ptr(), k.shape[0], k.stride(0), kc.shape[0], kc.stride(0))
+                    assert rc == 0, rc
+                return go
+            return [call(layer) for layer in range(L)]
+        for r in range(wl.R):  # eager pass: the rows land where our store puts them
+            for fn in layer_calls(r):
+                fn()
+        torch.cuda.synchronize()
+        s = wl.steps[wl.R - 1]
+        slots = s.out.slot_mapping
+        for layer in range(L):
+            assert torch.equal(wl.k_pool[layer].index_select(0, slots), s.k[layer])
+        n = max(8, min(64, args.steps))
+        us = per_launch_us(wl.R, layer_calls, n, reps=2)
+        nbytes = wl.b0.store_bytes()
+        gbs = nbytes / (us * 1e-6) / 1e9
+        return {"workload": wl.desc["workload"], "launches_per_step": L, "us_per_step": round(us, 3),
+                "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+                "kernel": "StoreKVCacheKernel<2048,128,bfloat16,false> (reference source, sm_100a)",
+                "timing": f"{n} steps of {L} per-layer launches in one CUDA graph, inputs rotating over {wl.R} sets",
+                "checked": "pool rows at the slots equal the input rows"}
+    finally:
+        wl.release()
+
+
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
-HOST_ROTATE_BYTES = 600e6  # host input sets cycled through: more than a server's last-level cache
-
-
-def host_step_setup(b: workloads.Batch, pool_gb: float = 4.0):
-    """Host copies of the batch for the CPU arm: the pool scaled down to
-    pool_gb (same row and page size; read-only pages alias, written pages
-    stay unique) and enough input sets -- K/V rows as raw bf16 bits, page
-    tables with their own page ids -- that one pass over them (> 600 MB) does
-    not fit a CPU's last-level cache, as the GPU arm rotates past its L2."""
-    P = max(workloads.pool_pages_for(pool_gb * 1e9, b.layers, b.row_bytes, b.page_size), b.tokens + 1)
-    per_set = 2 * b.layers * b.tokens * b.row_bytes
-    R = max(1, min(16, int(math.ceil(HOST_ROTATE_BYTES / per_set))))
-    sets = []
-    for r in range(R):
-        if b.name == "llama3_decode":
-            hb = workloads.llama3_decode(P, batch=b.batch, kv_heads=b.kv_heads, layers=b.layers, seed_pages=2 + r)
-        elif b.name == "ragged_prefill":
-            hb = workloads.ragged_prefill(P, requests=b.batch, kv_heads=b.kv_heads, layers=b.layers,
-                                          seed_pages=2 + r)
-        else:
-            hb = b
-        E = hb.kv_heads * hb.head_dim
-        rng = np.random.default_rng(r)
-        n = hb.layers * hb.tokens * E
-        k = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
-        v = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
-        sets.append((hb, k, v))
-    hb = sets[0][0]
-    pool = np.zeros((2, hb.layers, hb.num_pages * hb.page_size, hb.kv_heads * hb.head_dim), np.uint16)
-    return sets, pool
-
-
-def host_step(hb, pool, k, v, threads):
-    from oracle import kvpath as orc
-    out = orc.build_index(hb.prior_len, hb.new_len, hb.page_table, hb.page_size, num_pages=hb.num_pages)
-    orc.store(k, v, pool[0], pool[1], out["slot_mapping"], num_slots=pool.shape[2], threads=threads)
-
-
 def run_reference(args, world, rank):
-    """CPU arm: the path on the host cores (rank 0 only)."""
+    """The reference arm: the path on the host cores (rank 0 only), as
+    libtorch CPU ops; beside it the C port, the reference's own host index
+    helper and the reference's own GPU store kernel."""
     if rank != 0:
         return
-    from oracle import kvpath as orc
     batches, desc = make_batches(args.workload, 1, 150e9, 1)
     b = batches[0]
-    threads = orc.max_threads()
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
     sets, pool = host_step_setup(b)
+    th = TorchHost(sets, pool)
     hb = sets[0][0]
     times = []
     for it in range(args.warmup + args.steps):
-        s_hb, k, v = sets[it % len(sets)]
         t0 = time.perf_counter()
-        host_step(s_hb, pool, k, v, threads)
+        th.step(it)
         if it >= args.warmup:
             times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
@@ -404,142 +706,121 @@ def run_reference(args, world, rank):
         "config": desc,
         "tokens_per_s": round(hb.tokens / per, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"each step: index build + store of {hb.name} (B={hb.batch}, N={hb.tokens}, "
-                                   f"L={hb.layers}) into a {pool.nbytes / 1e9:.1f} GB host pool by the C oracle, "
-                                   f"inputs rotating over {len(sets)} sets; the reference's store exists only as "
-                                   "a CUDA kernel"},
+                         "hardware_concurrency": os.cpu_count(),
+                         "sample": f"each step: index arrays of {hb.name} (B={hb.batch}, N={hb.tokens}, L={hb.layers}) "
+                                   "by libtorch CPU ops, then index_copy_ of every layer's K and V rows into the "
+                                   f"[pages * page_size, row] views of a {pool.nbytes / 1e9:.1f} GB host pool, inputs "
+                                   f"rotating over {len(sets)} sets; the reference's store exists only as a CUDA "
+                                   "kernel, so its semantics run as libtorch CPU ops"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    from oracle import kvpath as orc
+    cthreads = orc.max_threads()
+
+    def c_step(r):
+        s_hb, k, v = sets[r % len(sets)]
+        c_port_step(s_hb, pool, k, v, cthreads)
+    for r in range(len(sets)):
+        c_step(r)
+    per_c, reps = timed_host_steps(c_step, 3.0)
+    line["c_port"] = {"value": round(hb.store_bytes() / per_c / 1e9, 3), "unit": "GB/s", "cores": cthreads,
+                      "ms_per_step": round(per_c * 1e3, 4), "steps": reps,
+                      "what": "the C oracle's index build + pthread store, same sets and pool"}
     mk = ref_make2d_us(b, max_seconds=5.0)
     if mk:
         line["reference_make2dindices"] = mk
+    if not args.no_ref_gpu:
+        peak, _ = load_peaks()
+        try:
+            line["reference_gpu_store"] = ref_gpu_store(args, b, peak)
+        except Exception as e:  # report, do not lose the CPU line
+            line["reference_gpu_store"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(line), flush=True)
 
 
 def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
-    free, total = torch.cuda.mem_get_info(dev)
     shape_world = 1 if args.replicas else world  # replicas: every rank runs the one-GPU shapes
-    R, pool_bytes, per_set = plan(args, shape_world, free)
-    batches, desc = make_batches(args.workload, shape_world, pool_bytes, R)
-    b0 = batches[0]
-    P = b0.num_pages
-    S = P * b0.page_size
-    E = b0.kv_heads * b0.head_dim
-    L = b0.layers
-    pool = torch.empty((2, L, S, E), dtype=torch.bfloat16, device=dev)
-    k_pool, v_pool = pool[0], pool[1]
-    steps = [Step(b, dev, seed=1000 * rank + r) for r, b in enumerate(batches)]
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    step_bytes = b0.step_bytes()
-    store_bytes = b0.store_bytes()
-    index_bytes = b0.index_bytes()
-    fused = args.path == "fused"
-    step_mode = os.environ.get("YL_STEP_MODE", "pdl") if fused else "separate calls"
-    index_launches = 2 if b0.batch > 16384 else 1  # the two-launch index form for huge batches
-    launches_per_step = 1 if step_mode == "fused" and b0.batch <= 4096 else index_launches + 1
-
-    def step_launches(r):
-        s = steps[r]
-        if fused:
-            return [lambda: s.fused(k_pool, v_pool, err)]
-        return [lambda: s.index(err), lambda: s.store(k_pool, v_pool, err)]
-
-    # warm-up: eager steps through the public API
-    for w in range(args.warmup):
-        for fn in step_launches(w % R):
-            fn()
-    torch.cuda.synchronize()
-    assert int(err.item()) == 0, f"device error word {int(err.item()):#x} during warm-up"
-
-    # timed steps: a graph of C steps replayed q times + a remainder graph
-    K = args.steps
-    C = min(K, args.chunk)
-    q, rem = divmod(K, C)
-    g_main = capture([j % R for j in range(C)], step_launches)
-    g_rem = capture([(q * C + j) % R for j in range(rem)], step_launches) if rem else None
-    g_main.replay()  # untimed graph warm-up
-    torch.cuda.synchronize()
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(q):
-            g_main.replay()
-        if g_rem is not None:
-            g_rem.replay()
-        end.record()
-        torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
-    ms_max = reduce_max(ms, world)
-    assert int(err.item()) == 0, f"device error word {int(err.item()):#x}"
-    del g_main, g_rem
-
-    # each kernel on its own, back to back in a graph: the standalone index
-    # build, the all-layer store, and the reference's one store per layer
-    n_sep = min(K, 256)
-    index_us = per_launch_us(R, lambda r: [lambda: steps[r].index(err)], n_sep)
-    store_us = per_launch_us(R, lambda r: [lambda: steps[r].store(k_pool, v_pool, err)], n_sep)
-    layer_us = per_launch_us(R, lambda r: [(lambda l: (lambda: steps[r].store_layer(l, k_pool, v_pool, err)))(
-        layer) for layer in range(L)], min(K, 16)) / L
-    assert int(err.item()) == 0, f"device error word {int(err.item()):#x}"
-
-    # every collective runs on all ranks, in the same order, before rank 0 reports
-    per_step_s = ms_max / 1e3 / K
-    total_store = reduce_sum(float(store_bytes), world)
-    total_step = reduce_sum(float(step_bytes), world)
-    value = total_store / per_step_s / 1e9
-    tokens_global = b0.tokens  # every rank stores its head slice of every token
     peak, peak_kind = load_peaks()
-    achieved = store_bytes / (store_us * 1e-6) / 1e9
-
+    wl = Workload(args.workload, args, shape_world, dev, rank)
+    desc = dict(wl.desc)
+    K = args.steps
+    clocks = ClockSampler(local)  # samples during the timed region only
+    m = measure(wl, args, world, K, args.warmup, clocks)
+    n_layer = min(K, 16)
+    L = wl.b0.layers
+    layer_us = reduce_max(per_launch_us(wl.R, lambda r: [(lambda l: (lambda: wl.steps[r].store_layer(
+        l, wl.k_pool, wl.v_pool, wl.err)))(layer) for layer in range(L)], n_layer), world) / L
+    wl.check_err("in the per-layer store timing")
     e2e = None
     if not args.no_e2e:
-        if per_set <= 4e9:
-            e2e = run_e2e(args, steps[:min(R, 2)], k_pool, v_pool, err, world)
+        if wl.per_set <= 4e9:
+            e2e = run_e2e(args, wl.steps[:min(wl.R, 2)], wl.k_pool, wl.v_pool, wl.err, world)
         else:
-            e2e = {"value": None, "unit": "GB/s", "skipped": f"one step's inputs are {per_set / 1e9:.0f} GB"}
+            e2e = {"value": None, "unit": "GB/s", "skipped": f"one step's inputs are {wl.per_set / 1e9:.0f} GB"}
+    b0 = wl.b0
+    wl.release()
 
+    # the other workloads, every rank, in the same order
+    extras = {}
+    names = [n for n in (args.extras.split(",") if args.extras is not None else DEFAULT_EXTRAS) if n]
+    for name in names:
+        if name == args.workload:
+            continue
+        sub = Workload(name, args, shape_world, dev, rank)
+        try:
+            sm = measure(sub, args, world, min(K, args.extra_steps), 3)
+            extras[name] = summarize(sm, sub.desc, world, peak)
+            extras[name]["gpu_launches_per_step"] = sm["launches_per_step"]
+        finally:
+            sub.release()
+
+    per_step_s = m["step_us"] * 1e-6
+    total_store = reduce_sum(float(m["store_bytes"]), world)
+    value = total_store / per_step_s / 1e9
     if rank != 0:
         return
+    step_gbs = m["step_bytes"] / per_step_s / 1e9
+    store_gbs = m["store_bytes"] / (m["store_us"] * 1e-6) / 1e9
+    traffic = args.traffic if args.traffic is not None else STEP_TRAFFIC_NCU.get((args.workload, shape_world))
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": round(m["step_us"] / 1e3, 5), "higher_is_better": True,
         "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded lengths and fragmented page tables, K/V N(0,1) cast to bf16",
         "config": dict(desc, parallelism=(f"replicas x{world}" if args.replicas else f"kv-head shard x{world}")
                        if world > 1 else "single GPU",
-                       path=(f"yl_kv_step ({step_mode})" if fused else "build_index + store_kv_cache"),
-                       l2=f"inputs rotate over {R} sets ({R * per_set / 1e6:.0f} MB > 2 x L2), "
+                       path=(f"yl_kv_step ({os.environ.get('YL_STEP_MODE', 'pdl')})" if wl.fused
+                             else "build_index + store_kv_cache"),
+                       l2=f"inputs rotate over {wl.R} sets ({wl.R * wl.per_set / 1e6:.0f} MB > 2 x L2), "
                           "distinct destination slots per set"),
-        "tokens_per_s": round(tokens_global / per_step_s, 1),
+        "tokens_per_s": round(m["tokens"] / per_step_s, 1),
         "pct_hbm": round(100 * value / (peak * world), 2),
-        "index_build_us": round(index_us, 3),
-        "step_us": round(ms_max * 1e3 / K, 3),
-        "step_gbs": round(total_step / per_step_s / 1e9, 1),
-        "store_us": round(store_us, 3),
-        "store_gbs": round(achieved, 1),
-        "index_gbs": round(index_bytes / (index_us * 1e-6) / 1e9, 1),
+        "step_us": round(m["step_us"], 3),
+        "index_build_us": round(m["index_us"], 3),
+        "index_gbs": round(m["index_bytes"] / (m["index_us"] * 1e-6) / 1e9, 1),
+        "verified": m["verified"],
+        "roofline": {"bound": "hbm",
+                     "kernel": "the timed step (yl_kv_step: index build + store of every layer)",
+                     "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(step_gbs / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} hbm_gbs (copy)",
+                     "algorithmic_bytes_per_launch": m["step_bytes"],
+                     "launch_us": round(m["step_us"], 3),
+                     "timing": f"{K} steps as CUDA-graph replays behind a device delay, events on the launching "
+                               "stream, max over ranks",
+                     "store_kernel": {"us": round(m["store_us"], 3), "achieved": round(store_gbs, 1),
+                                      "frac": round(store_gbs / peak, 4),
+                                      "algorithmic_bytes_per_launch": m["store_bytes"],
+                                      "timing": "the all-layer store alone, back-to-back launches in one graph"}},
         "per_layer_store": {"launches_per_step": L, "us_per_launch": round(layer_us, 3),
-                            "gbs": round(store_bytes / L / (layer_us * 1e-6) / 1e9, 1)},
-        "roofline": {"bound": "hbm", "kernel": "store_rows_kernel (all layers of a step, one launch)",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4),
-                     "traffic": args.traffic if args.traffic is not None else STORE_TRAFFIC_NCU.get(
-                         (args.workload, shape_world)),
-                     "peak_source": f"{peak_kind} hbm_gbs (copy)", "algorithmic_bytes_per_launch": store_bytes,
-                     "launch_us": round(store_us, 3),
-                     "timing": f"{n_sep} back-to-back launches in one CUDA graph, events around the replays",
-                     "timed_step_kernels": "build_index_kernel, then the store (for decode batches "
-                                           "store_rows_self_kernel / store_tokens_self_kernel, which compute "
-                                           "their own slots and run beside the index build)"},
-        "gpu_launches": K * launches_per_step,
+                            "gbs": round(m["store_bytes"] / L / (layer_us * 1e-6) / 1e9, 1)},
+        "gpu_launches": K * m["launches_per_step"],
         "clocks": clocks.summary(),
+        "workloads": extras,
     }
+    if world > 1:
+        line["per_rank_step_us"] = rank_stats(m["per_rank_step_us"])
     if e2e is not None:
         line["e2e"] = e2e
     if not args.no_gather:
@@ -839,6 +1120,8 @@ def _run_e2e(args, steps, k_pool, v_pool, err, world):
     total = reduce_sum(float(b.store_bytes()), world)
     return {"value": round(total / per / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": 4, "steps": E, "ms_per_step": round(ms / E, 4),
+            "h2d_gbs": round(h2d / per / 1e9, 2),
+            "bound": "the step's host-to-device copies (PCIe): h2d_gbs is their achieved rate",
             "path": "pinned host -> device copies (K and V on two copy streams), yllang_b200.kv_step, "
                     "error word -> host"}
 
@@ -866,7 +1149,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--traffic", type=float, default=None,
-                    help="ncu DRAM bytes per store launch (from the committed profile) to report")
+                    help="ncu DRAM bytes per timed step (from the committed profile) to report")
+    ap.add_argument("--extras", default=None,
+                    help="comma-separated workloads measured as sub-objects (default: " + ",".join(DEFAULT_EXTRAS)
+                         + "; empty: none)")
+    ap.add_argument("--extra-steps", type=int, default=20, help="timed steps of each sub-workload")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="reference arm: skip timing the reference's own GPU store kernel")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least three untimed steps
     world, rank, local = dist_setup()

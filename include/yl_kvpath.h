@@ -73,6 +73,7 @@ typedef enum yl_status {
 #define YL_DEVERR_POSITION_RANGE  0x800u /* qkv store: position outside [0, max_position)     */
 #define YL_DEVERR_POOL_EMPTY      0x1000u /* reserve: fewer free pages than the batch needs  */
 #define YL_DEVERR_POOL_OVERFLOW   0x2000u /* release: more pages than the free list holds    */
+#define YL_DEVERR_DUPLICATE_ROW   0x4000u /* reserve, release: one table row named twice     */
 
 /*
  * Store (replaces yllang::StoreKVCache<kElementSize>,
@@ -306,9 +307,9 @@ YL_API int yl_qkv_norm_rope_store(const yl_qkv_store_args *args, cudaStream_t st
  * Release appends the pages of the given rows (ceil(num_tokens[r] /
  * page_size) each, in row order) to the list and sets those table entries to
  * -1.  Both are all-or-nothing: any bad input (negative length, row outside
- * the table, more pages than a row holds, a page id outside [0, capacity))
- * or a pool that cannot satisfy the call sets an error bit and changes
- * nothing.  One CTA runs each call; calls on one stream are ordered, calls on
+ * the table, one row named twice in the call, more pages than a row holds, a
+ * page id outside [0, capacity)) or a pool that cannot satisfy the call sets
+ * an error bit and changes nothing.  One CTA runs each call; calls on one stream are ordered, calls on
  * different streams on one pool race.  No counterpart kernel in the
  * reference, whose allocator is host code.
  */

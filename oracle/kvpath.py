@@ -41,6 +41,7 @@ INDEX_RANGE = 0x400
 POSITION_RANGE = 0x800
 POOL_EMPTY = 0x1000
 POOL_OVERFLOW = 0x2000
+DUPLICATE_ROW = 0x4000
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -338,3 +339,44 @@ def py_build_index(prior_len, new_len, page_table, page_size, table_index=None):
         "qo_indptr": np.array(qo_indptr, np.int32),
         "slot_mapping": np.array(slots, np.int64),
     }
+
+
+# ---------------------------------------------------------------------------
+# libtorch restatement on CPU tensors: the reference's store and the index
+# work of NextBatch expressed as libtorch CPU ops, which is how the reference's
+# host code runs its tensor work.  The CPU baseline times it on all host
+# threads; tests check it against the C oracle.
+# ---------------------------------------------------------------------------
+def torch_build_index(prior_len, new_len, page_table, page_size: int) -> dict:
+    """The five index arrays of a batch with valid inputs (lengths >= 0, rows
+    long enough) from int32 CPU tensors, vectorised over the batch: page
+    counts and their cumulative sums (the per-request ranges of
+    batch_manager.h:97-107), each sequence's page-table prefix (the load
+    indices, :106) and the slots of its new tokens (out_loc, :109-110)."""
+    import torch
+
+    prior = prior_len.to(torch.int64).clamp(min=0)
+    new = new_len.to(torch.int64).clamp(min=0)
+    total = prior + new
+    W = page_table.shape[1]
+    pages = torch.clamp((total + page_size - 1) // page_size, max=W)
+    zero = torch.zeros(1, dtype=torch.int64)
+    kv_indptr = torch.cat([zero, pages.cumsum(0)])
+    qo_indptr = torch.cat([zero, new.cumsum(0)])
+    last = torch.where(pages == 0, torch.zeros_like(total), (total - 1) % page_size + 1)
+    kv_indices = page_table[:prior.shape[0]][torch.arange(W)[None, :] < pages[:, None]]
+    seq = torch.repeat_interleave(torch.arange(prior.shape[0]), new)
+    pos = prior[seq] + torch.arange(seq.shape[0]) - qo_indptr[seq]
+    slots = page_table[seq, pos // page_size].to(torch.int64) * page_size + pos % page_size
+    return {"kv_indptr": kv_indptr.to(torch.int32), "kv_indices": kv_indices.to(torch.int32),
+            "kv_last_page_len": last.to(torch.int32), "qo_indptr": qo_indptr.to(torch.int32), "slot_mapping": slots}
+
+
+def torch_store(k, v, k_pool, v_pool, slots) -> None:
+    """StoreKVCacheKernel's k_cache[idx[i]] = k[i] (store_kv_cache.cu:60-72)
+    per layer, as MHAKVCache::StoreKV calls it (mha_kvcache.h:76-86), with
+    libtorch's CPU index_copy_ on the [pages * page_size, row] pool views:
+    k, v [L, N, E], pools [L, S, E], slots int64 [N]."""
+    for layer in range(k.shape[0]):
+        k_pool[layer].index_copy_(0, slots, k[layer])
+        v_pool[layer].index_copy_(0, slots, v[layer])

@@ -27,6 +27,7 @@
  * the GPU); threads == 1 is strictly sequential (last writer wins).
  */
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <pthread.h>
@@ -240,8 +241,9 @@ int64_t oracle_gather_rows(const uint8_t *table, uint8_t *out, const void *indic
  * list keeps the rest (the reference keeps slice(0, size), a defect); the
  * pages go into the request's page-table row after the pages it holds
  * (WritePageTable, :148-155, meant for the page table).  All-or-nothing:
- * returns error bits and changes nothing when any request is invalid or the
- * list is short.  Bits as in yl_kvpath.h.
+ * returns error bits and changes nothing when any request is invalid (a
+ * page-table row named twice included) or the list is short.  Bits as in
+ * yl_kvpath.h.
  */
 #define O_NEGATIVE_LEN 0x20u
 #define O_TABLE_ROW 0x80u
@@ -249,6 +251,24 @@ int64_t oracle_gather_rows(const uint8_t *table, uint8_t *out, const void *indic
 #define O_PAGE_RANGE 0x2u
 #define O_POOL_EMPTY 0x1000u
 #define O_POOL_OVERFLOW 0x2000u
+#define O_DUPLICATE_ROW 0x4000u
+
+/* 0x4000 when a valid row in [0, num_rows) appears twice in rows[0, n):
+ * two sequences of one call would write one page-table row (reserve), or one
+ * row's pages would enter the free list twice (release). */
+static uint32_t o_duplicate_rows(const int32_t *rows, int32_t n, int32_t num_rows) {
+  if (rows == NULL || n < 2 || num_rows <= 0) return 0;
+  unsigned char *seen = (unsigned char *)calloc((size_t)num_rows, 1);
+  uint32_t err = 0;
+  for (int32_t i = 0; seen && i < n && !err; ++i) {
+    const int32_t r = rows[i];
+    if (r < 0 || r >= num_rows) continue;
+    if (seen[r]) err = O_DUPLICATE_ROW;
+    seen[r] = 1;
+  }
+  free(seen);
+  return err;
+}
 
 static int64_t o_pages_for(int64_t tokens, int32_t ps) { return (tokens + ps - 1) / ps; }
 
@@ -265,6 +285,7 @@ uint32_t oracle_reserve_pages(int32_t *free_pages, int32_t *free_count, int64_t 
     if (need > max_pages) { err |= O_ROW_OVERFLOW; continue; }
     total += need - o_pages_for(prior[i], page_size);
   }
+  err |= o_duplicate_rows(table_index, batch, num_rows);
   const int64_t n = *free_count;
   if (!err && (n < 0 || n > capacity || total > n)) err |= O_POOL_EMPTY;
   for (int64_t k = n - total; !err && k < n; ++k)
@@ -283,7 +304,8 @@ uint32_t oracle_reserve_pages(int32_t *free_pages, int32_t *free_count, int64_t 
 }
 
 /* Release: rows in order append their ceil(tokens / page_size) pages to the
- * free list and clear those table entries to -1; all-or-nothing. */
+ * free list and clear those table entries to -1; all-or-nothing (a row named
+ * twice is invalid). */
 uint32_t oracle_release_pages(int32_t *free_pages, int32_t *free_count, int64_t capacity, int32_t *table,
                               int64_t stride, int32_t num_rows, int32_t max_pages, const int32_t *rows,
                               const int32_t *num_tokens, int32_t page_size, int32_t count) {
@@ -300,6 +322,7 @@ uint32_t oracle_release_pages(int32_t *free_pages, int32_t *free_count, int64_t 
     }
     total += c;
   }
+  err |= o_duplicate_rows(rows, count, num_rows);
   const int64_t n = *free_count;
   if (!err && (n < 0 || n + total > capacity)) err |= O_POOL_OVERFLOW;
   if (err) return err;

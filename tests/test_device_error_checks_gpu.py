@@ -71,6 +71,23 @@ assert pool.free_count() == 4 and bool((pt == -1).all())
 cpool = C.DevicePagePool(4, "cuda:0")
 raises(lambda: cpool.Reserve(pt, torch.zeros(2, **i32), torch.tensor([64, 64], **i32), 16), "POOL_EMPTY",
        C.PanicError)
+
+# calls on a side stream: the private word is zeroed on that stream and read
+# after it finishes, so a kernel queued behind a long one is still checked
+side = torch.cuda.Stream(dev)
+big = torch.empty(1 << 28, dtype=torch.uint8, device=dev)
+side.wait_stream(torch.cuda.current_stream(dev))
+for _ in range(3):
+    with torch.cuda.stream(side):
+        big.random_(0, 255)  # keeps the side stream busy past the current stream's work
+    raises(lambda: yl.store_kv_cache(k, v, kc, vc, bad, stream=side), "SLOT_RANGE", yl.PanicError)
+    raises(lambda: yl.gather_rows(torch.tensor([1, 10], device=dev), w, stream=side), "INDEX_RANGE",
+           yl.PanicError)
+    yl.store_kv_cache(k, v, kc, vc, ok, stream=side)
+with torch.cuda.stream(side):
+    rng = torch.tensor([[0, 0, 3], [100, 2, 4]], dtype=torch.int64, device=dev)
+flat = yl.make_2d_indices(rng, stream=side)
+assert flat.tolist() == [0, 1, 2, 102, 103]
 torch.cuda.synchronize()
 print("device error checks ok")
 """

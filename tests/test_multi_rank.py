@@ -49,6 +49,7 @@ def _rank_main(rank, world, port, out_dir):
         moved = sharding.sum_over_ranks(float(ks.nbytes + vs.nbytes))
         mine = float(ks.nbytes + vs.nbytes)
         slowest = sharding.max_over_ranks(float(rank + 1))
+        per_rank = sharding.gather_over_ranks(float(10 + rank))
         mine32 = torch.from_numpy(pool_k).view(torch.int32)  # gloo gathers no int16
         parts = [torch.zeros_like(mine32) for _ in range(world)]
         dist.all_gather(parts, mine32)
@@ -60,7 +61,8 @@ def _rank_main(rank, world, port, out_dir):
                       idx["slot_mapping"], num_slots=S)
             gathered = torch.cat([p.view(L, S, -1, D) for p in parts], dim=2).reshape(L, S, H * D).numpy()
             np.save(os.path.join(out_dir, "ok.npy"),
-                    np.array([np.array_equal(gathered, full_k), moved == world * mine, slowest == world]))
+                    np.array([np.array_equal(gathered, full_k), moved == world * mine, slowest == world,
+                              per_rank == [10.0 + r for r in range(world)]]))
     finally:
         dist.destroy_process_group()
 
@@ -70,7 +72,7 @@ def test_head_shard_two_ranks(tmp_path):
     mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     ok = np.load(tmp_path / "ok.npy")
-    assert ok.tolist() == [True, True, True]
+    assert ok.tolist() == [True, True, True, True]
 
 
 def test_head_range_rules():
@@ -83,3 +85,4 @@ def test_head_range_rules():
     x = torch.arange(2 * 3 * 8 * 4).view(2, 3, 8, 4)
     assert torch.equal(sharding.head_slice(x, 1, 2), x[:, :, 4:8, :].reshape(2, 3, 16))
     assert sharding.max_over_ranks(3.5) == 3.5  # no process group: identity
+    assert sharding.gather_over_ranks(2.5) == [2.5]

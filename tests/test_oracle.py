@@ -355,7 +355,14 @@ def test_page_pool_oracle_is_all_or_nothing():
     assert pool.reserve(table, [0, 0], [8, 4], 4) == 0
     # request 0 takes the tail [8, 9], request 1 the next tail [7]
     assert table[0, :2].tolist() == [8, 9] and table[1, :1].tolist() == [7] and pool.count[0] == 7
-    assert pool.release(table, [0, 0], [8, 8], 4) == orc.POOL_OVERFLOW and pool.count[0] == 7  # 7 + 4 > 10
+    before = table.copy()
+    assert pool.reserve(table, [0, 0], [4, 4], 4, table_index=[2, 2]) == orc.DUPLICATE_ROW  # row 2 twice
+    assert pool.release(table, [0, 0], [8, 8], 4) == orc.DUPLICATE_ROW  # row 0's pages would enter twice
+    assert np.array_equal(table, before) and pool.count[0] == 7
+    full = orc.PagePool(10, free_pages=np.arange(9, dtype=np.int32))
+    assert full.release(table, [0], [8], 4) == orc.POOL_OVERFLOW and full.count[0] == 9  # 9 + 2 > 10
+    assert pool.release(table, [1, 0], [4, 8], 4) == 0 and pool.free_list().tolist() == list(range(7)) + [7, 8, 9]
+    assert pool.reserve(table, [0, 0], [8, 4], 4) == 0 and pool.count[0] == 7  # back to the state above
     assert pool.release(table, [0], [8], 4) == 0 and pool.free_list().tolist() == list(range(7)) + [8, 9]
     assert pool.release(table, [1], [4], 4) == 0 and pool.free_list().tolist() == list(range(7)) + [8, 9, 7]
     bad = np.array([[5, 11, -1, -1, -1, -1, -1, -1]] * 3, np.int32)
@@ -392,3 +399,30 @@ def test_host_kvcache_manager_matches_page_pool_oracle():
         lens += new
     assert np.array_equal(m.HostPageTable().numpy(), table)
     assert m.RemainingPageCount() == int(pool.count[0])
+
+
+@pytest.mark.parametrize("which", ["cpu_ref", "decode", "mixed_ps1", "mixed_ps64"])
+def test_torch_restatement_matches_c_oracle(which):
+    """The libtorch CPU restatement the CPU baseline times gives the C oracle's
+    index arrays and pool bytes."""
+    import torch
+    from yllang_b200 import workloads
+    b = {"cpu_ref": lambda: workloads.cpu_ref(),
+         "decode": lambda: workloads.llama3_decode(80000, layers=2),
+         "mixed_ps1": lambda: workloads.mixed(20000, page_size=1, head_dim=64, layers=2),
+         "mixed_ps64": lambda: workloads.mixed(6000, page_size=64, head_dim=256, layers=2)}[which]()
+    want = orc.build_index(b.prior_len, b.new_len, b.page_table, b.page_size)
+    got = orc.torch_build_index(torch.from_numpy(b.prior_len), torch.from_numpy(b.new_len),
+                                torch.from_numpy(b.page_table), b.page_size)
+    for name in got:
+        assert np.array_equal(got[name].numpy(), want[name]), name
+    S, E = b.num_pages * b.page_size, 64
+    rng = np.random.default_rng(5)
+    k = rng.integers(-2**15, 2**15, (b.layers, b.tokens, E), dtype=np.int16)
+    v = rng.integers(-2**15, 2**15, (b.layers, b.tokens, E), dtype=np.int16)
+    pools = rng.integers(-2**15, 2**15, (2, b.layers, S, E), dtype=np.int16)
+    want_pools = pools.copy()
+    orc.store(k, v, want_pools[0], want_pools[1], want["slot_mapping"])
+    tp = torch.from_numpy(pools)
+    orc.torch_store(torch.from_numpy(k), torch.from_numpy(v), tp[0], tp[1], got["slot_mapping"])
+    assert np.array_equal(tp.numpy(), want_pools)

@@ -68,10 +68,23 @@ def test_reserve_release_errors_change_nothing(cuda):
     pool.reserve(table, t([0, 0]), t([8, 4]), ps, error_word=err)
     free, got = _state(pool, table)
     assert got[0, :2].tolist() == [8, 9] and got[1, :1].tolist() == [7] and free.tolist() == list(range(7))
+    before = table.cpu().numpy()
     err.zero_()
-    pool.release(table, t([0, 0]), t([8, 8]), ps, error_word=err)  # 7 + 4 > 10
+    pool.reserve(table, t([0, 0]), t([4, 4]), ps, table_index=t([2, 2]), error_word=err)  # row 2 twice
     free, got = _state(pool, table)
-    assert int(err.item()) == yl.DEVERR_POOL_OVERFLOW and free.tolist() == list(range(7))
+    assert int(err.item()) == yl.DEVERR_DUPLICATE_ROW and free.tolist() == list(range(7))
+    assert np.array_equal(got, before)
+    err.zero_()
+    pool.release(table, t([0, 0]), t([8, 8]), ps, error_word=err)  # row 0's pages would enter the list twice
+    free, got = _state(pool, table)
+    assert int(err.item()) == yl.DEVERR_DUPLICATE_ROW and free.tolist() == list(range(7))
+    assert np.array_equal(got, before)
+    full = yl.DevicePagePool(P, cuda, free_pages=torch.arange(9, dtype=torch.int32))
+    err.zero_()
+    full.release(table, t([0]), t([8]), ps, error_word=err)  # 9 + 2 > 10
+    free, got = _state(full, table)
+    assert int(err.item()) == yl.DEVERR_POOL_OVERFLOW and free.tolist() == list(range(9))
+    assert np.array_equal(got, before)
     pool.release(table, t([0, 1]), t([8, 4]), ps)
     free, got = _state(pool, table)
     assert free.tolist() == list(range(7)) + [8, 9, 7] and (got == -1).all()
@@ -82,6 +95,55 @@ def test_reserve_release_errors_change_nothing(cuda):
     small.release(bad, t([0]), t([8]), ps, error_word=err)
     torch.cuda.synchronize()
     assert int(err.item()) == yl.DEVERR_PAGE_RANGE and small.free_count() == 6
+
+
+@pytest.mark.parametrize("case", ["reserve", "release"])
+@pytest.mark.parametrize("spread", [False, True])
+def test_duplicate_rows_change_nothing(cuda, case, spread):
+    """A table row named twice in one call (batches over several 1024-thread
+    chunks; rows within one bitmap window, or spread over a 700,000-row table
+    so the check walks several windows) sets DEVERR_DUPLICATE_ROW and leaves
+    the free list and the table as they were; the same batch without the
+    repeat goes through, as in the oracle."""
+    rng = np.random.default_rng(11 + int(spread))
+    B, ps, W = 2500, 16, 4
+    R = 700_000 if spread else B + 50
+    P = 4 * B + 100
+    rows = (np.sort(rng.choice(R, size=B, replace=False)) if spread else rng.permutation(R)[:B]).astype(np.int32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(cuda)
+    table = torch.full((R, W), -1, dtype=torch.int32, device=cuda)
+    otable = np.full((R, W), -1, np.int32)
+    pool, opool = yl.DevicePagePool(P, cuda), orc.PagePool(P)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    zeros = np.zeros(B, np.int32)
+    lens = rng.integers(1, W * ps + 1, B).astype(np.int32)
+    if case == "release":  # fill the rows first
+        pool.reserve(table, t(zeros), t(lens), ps, table_index=t(rows), error_word=err)
+        assert opool.reserve(otable, zeros, lens, ps, table_index=rows) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    dup = rows.copy()
+    dup[B - 3] = dup[5]  # far apart: first and last windows when spread
+    free0, table0 = _state(pool, table)
+    if case == "reserve":
+        pool.reserve(table, t(zeros), t(lens), ps, table_index=t(dup), error_word=err)
+        want = opool.reserve(otable, zeros, lens, ps, table_index=dup)
+    else:
+        pool.release(table, t(dup), t(lens), ps, error_word=err)
+        want = opool.release(otable, dup, lens, ps)
+    free, got = _state(pool, table)
+    assert want == yl.DEVERR_DUPLICATE_ROW and int(err.item()) == want
+    assert np.array_equal(free, free0) and np.array_equal(got, table0)
+    err.zero_()
+    if case == "reserve":
+        pool.reserve(table, t(zeros), t(lens), ps, table_index=t(rows), error_word=err)
+        assert opool.reserve(otable, zeros, lens, ps, table_index=rows) == 0
+    else:
+        pool.release(table, t(rows), t(lens), ps, error_word=err)
+        assert opool.release(otable, rows, lens, ps) == 0
+    free, got = _state(pool, table)
+    assert int(err.item()) == 0
+    assert np.array_equal(free, opool.free_list()) and np.array_equal(got, otable)
 
 
 def test_index_build_on_device_reserved_table(cuda):

@@ -28,7 +28,7 @@ from __future__ import annotations
 from ._abi import (DEVERR_INDICES_CAP, DEVERR_INDPTR_OVERFLOW, DEVERR_NEGATIVE_LEN, DEVERR_PAGE_RANGE,
                    DEVERR_INDEX_RANGE, DEVERR_ROW_OVERFLOW, DEVERR_SLOT_RANGE, DEVERR_SLOTS_CAP, DEVERR_TABLE_ROW,
                    DEVERR_POOL_EMPTY, DEVERR_POOL_OVERFLOW, DEVERR_POSITION_RANGE, DEVERR_TIMEOUT, DEVERR_TOKEN_COUNT,
-                   KVPathError, lib)
+                   DEVERR_DUPLICATE_ROW, KVPathError, lib)
 from .ops import (BatchIndex, DevicePagePool, PanicError, build_index, gather_rows, kv_step, make_2d_indices,
                   qkv_norm_rope_store, rope_cos_sin_cache, store_args, store_kv_cache)
 
@@ -39,6 +39,7 @@ __all__ = [
     "load_extension", "DEVERR_SLOT_RANGE", "DEVERR_PAGE_RANGE", "DEVERR_ROW_OVERFLOW", "DEVERR_INDICES_CAP",
     "DEVERR_SLOTS_CAP", "DEVERR_NEGATIVE_LEN", "DEVERR_INDPTR_OVERFLOW", "DEVERR_TABLE_ROW", "DEVERR_TOKEN_COUNT",
     "DEVERR_TIMEOUT", "DEVERR_INDEX_RANGE", "DEVERR_POSITION_RANGE", "DEVERR_POOL_EMPTY", "DEVERR_POOL_OVERFLOW",
+    "DEVERR_DUPLICATE_ROW",
 ]
 
 _ext = None

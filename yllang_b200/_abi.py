@@ -34,6 +34,7 @@ DEVERR_INDEX_RANGE = 0x400
 DEVERR_POSITION_RANGE = 0x800
 DEVERR_POOL_EMPTY = 0x1000
 DEVERR_POOL_OVERFLOW = 0x2000
+DEVERR_DUPLICATE_ROW = 0x4000
 
 ABI_VERSION = 1
 

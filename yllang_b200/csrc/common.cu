@@ -1,4 +1,5 @@
 // Host-side plumbing shared by the store and index entry points.
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -38,6 +39,17 @@ int sm_count() {
     g_sm_count[dev] = n;
   }
   return g_sm_count[dev];
+}
+
+uint64_t bulk_wait_limit_ns() {
+  static const uint64_t limit = [] {
+    const char *e = std::getenv("YL_BULK_WAIT_LIMIT_NS");
+    if (e == nullptr || *e == '\0') return kBulkWaitLimitNs;
+    char *end = nullptr;
+    const unsigned long long v = std::strtoull(e, &end, 10);
+    return (end != e && *end == '\0' && v > 0 && v <= kBulkWaitLimitNs) ? static_cast<uint64_t>(v) : kBulkWaitLimitNs;
+  }();
+  return limit;
 }
 
 }  // namespace ylk

@@ -37,6 +37,15 @@ inline int check_launch(const char *what) {
 
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count();
+
+// Bound of a bulk-copy kernel's wait for its own copies (mbarrier phase):
+// 2 s of %globaltimer, after which the waiting thread sets YL_DEVERR_TIMEOUT,
+// waits once more with the full bound so its copies land, and leaves.
+// YL_BULK_WAIT_LIMIT_NS (read once per process; 1 .. 2e9) lowers the first of
+// those waits in the store's and the step's bulk-copy kernels, so a test can
+// make it give up while the copies are still in flight.
+constexpr uint64_t kBulkWaitLimitNs = 2000000000ull;
+uint64_t bulk_wait_limit_ns();
 // Current device ordinal (cached per host thread would be wrong across
 // cudaSetDevice, so this is a plain query).
 int current_device();

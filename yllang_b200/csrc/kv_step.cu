@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kStepThreads, 3) kv_step_kernel(const __grid_c
 // CTA's share of the page arrays; then each staging thread derives its rows'
 // slots, waits for its rows, and bulk-stores them to the pool.
 constexpr int kTmaSlotsPerThread = 8;
-constexpr uint64_t kTmaWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kTmaWaitLimitNs = kBulkWaitLimitNs;  // 2 s
 constexpr size_t kTmaSmemMax = 232448;               // 227 KB, the B200 per-CTA maximum
 
 static size_t tma_header_bytes(int batch) {
@@ -164,9 +164,9 @@ __global__ void __launch_bounds__(kStepThreads, 1)
         if (plane == 0) write_slot(p.ix, token, slot[k]);  // layer 0's K rows publish the slot mapping
       }
     }
-    if (!mbar_wait_bounded(bar, parity, kTmaWaitLimitNs)) {
+    if (!mbar_wait_bounded(bar, parity, st.wait_limit_ns)) {
       raise_deverr(p.ix.error_word, YL_DEVERR_TIMEOUT);
-      mbar_wait_bounded(bar, parity, kTmaWaitLimitNs);
+      mbar_wait_bounded(bar, parity, kTmaWaitLimitNs);  // let this thread's loads land before leaving
       break;
     }
 #pragma unroll

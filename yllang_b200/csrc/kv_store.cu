@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(256) store_tokens_self_kernel(const __grid_con
 // only until those stores have read shared memory.
 constexpr int kTmaThreads = 256;
 constexpr int kTmaSlotsPerThread = 8;
-constexpr uint64_t kTmaWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kTmaWaitLimitNs = kBulkWaitLimitNs;  // 2 s
 constexpr size_t kTmaBarrierBytes = kTmaThreads * sizeof(uint64_t);
 
 template <typename SlotT>
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         slot[k] = load_slot<SlotT>(p.slots, first + sl - plane * p.by_tokens.d);
       }
     }
-    if (!mbar_wait_bounded(bar, parity, kTmaWaitLimitNs)) {
+    if (!mbar_wait_bounded(bar, parity, p.wait_limit_ns)) {
       raise_deverr(p.error_word, YL_DEVERR_TIMEOUT);
       mbar_wait_bounded(bar, parity, kTmaWaitLimitNs);  // let this thread's loads land before leaving
       break;
@@ -402,6 +402,7 @@ int prepare_store(const yl_store_args *a, bool need_slots, StorePlan &plan) {
   p.total_rows = static_cast<uint32_t>(total_rows);
   p.row_units = static_cast<uint32_t>(a->row_bytes / plan.unit);
   p.by_tokens = FastDiv(static_cast<uint32_t>(a->num_tokens));
+  p.wait_limit_ns = bulk_wait_limit_ns();
   return YL_OK;
 }
 

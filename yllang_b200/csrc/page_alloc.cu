@@ -2,7 +2,8 @@
 // KVCacheManager (src/include/kvcache/cache_manager.h:105-155) on the device.
 //
 // One CTA of 1024 threads per call.  Pass 1 walks the batch in chunks of
-// 1024 sequences (one per thread), checks every input and sums the pages the
+// 1024 sequences (one per thread), checks every input (a row named twice
+// included, through a shared-memory bitmap of the rows) and sums the pages the
 // call moves with a block scan; the call then either fails as a whole (error
 // bits, nothing written) or pass 2 walks the chunks again, recomputing each
 // sequence's offset from the running scan, and moves the page ids.  The
@@ -10,6 +11,7 @@
 // dependent loads, which is what a single CTA keeps short.
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -108,10 +110,61 @@ __device__ __forceinline__ uint32_t block_or(uint32_t err, uint32_t *s_err) {
   return *s_err;
 }
 
+// Rows of the table marked at once by the duplicate check: a 32 KB bitmap in
+// shared memory covers a window of 262,144 consecutive rows.
+constexpr int kRowBitmapWords = 8192;
+constexpr int64_t kRowWindow = 32ll * kRowBitmapWords;
+
+// YL_DEVERR_DUPLICATE_ROW (on every thread) when one row in
+// [0, num_rows) appears twice among rows[0, n): two sequences of a reserve
+// would fill one page-table row, or a release would put one row's pages on
+// the free list twice.  Rows outside the table are skipped (they carry their
+// own bit).  The bitmap walks the windows between the smallest and largest
+// row named, so a batch of a few thousand rows takes one window.  All
+// threads call it.
+__device__ uint32_t duplicate_rows(const int32_t *rows, int32_t n, int32_t num_rows, uint32_t *bits,
+                                   int32_t *s_lo, int32_t *s_hi) {
+  if (rows == nullptr || n < 2) return 0;
+  if (threadIdx.x == 0) {
+    *s_lo = INT32_MAX;
+    *s_hi = -1;
+  }
+  __syncthreads();
+  int32_t lo = INT32_MAX, hi = -1;
+  for (int32_t i = threadIdx.x; i < n; i += kPoolThreads) {
+    const int32_t r = rows[i];
+    if (r >= 0 && r < num_rows) {
+      lo = min(lo, r);
+      hi = max(hi, r);
+    }
+  }
+  if (hi >= 0) {
+    atomicMin(s_lo, lo);
+    atomicMax(s_hi, hi);
+  }
+  __syncthreads();
+  const int64_t first = *s_lo, last = *s_hi;
+  uint32_t dup = 0;
+  for (int64_t w0 = first; w0 <= last; w0 += kRowWindow) {
+    for (int k = threadIdx.x; k < kRowBitmapWords; k += kPoolThreads) bits[k] = 0;
+    __syncthreads();
+    for (int32_t i = threadIdx.x; i < n; i += kPoolThreads) {
+      const int64_t off = static_cast<int64_t>(rows[i]) - w0;
+      if (rows[i] < 0 || rows[i] >= num_rows || off < 0 || off >= kRowWindow) continue;
+      const uint32_t bit = 1u << (off & 31);
+      if (atomicOr(bits + (off >> 5), bit) & bit) dup = YL_DEVERR_DUPLICATE_ROW;
+    }
+    __syncthreads();  // the next window clears the bitmap
+  }
+  return __syncthreads_or(dup) ? YL_DEVERR_DUPLICATE_ROW : 0u;  // the same on every thread
+}
+
 __global__ void __launch_bounds__(kPoolThreads) reserve_pages_kernel(const __grid_constant__ PoolParams p) {
   __shared__ int64_t sums[32];
   __shared__ uint32_t s_err;
   __shared__ int64_t s_free;
+  __shared__ uint32_t s_rows[kRowBitmapWords];
+  __shared__ int32_t s_lo, s_hi;
   pdl_wait();  // lengths may be written by the kernel just before this one
   if (threadIdx.x == 0) {
     s_err = 0;
@@ -130,9 +183,13 @@ __global__ void __launch_bounds__(kPoolThreads) reserve_pages_kernel(const __gri
     block_exclusive_scan(lack, t, sums);
     total += t;
   }
-  if (threadIdx.x == 0 && (free_n < 0 || free_n > p.capacity || total > free_n)) err |= YL_DEVERR_POOL_EMPTY;
-  // the ids about to leave the list: free_pages[free_n - total, free_n)
-  if (block_or(err, &s_err) == 0) {
+  err |= duplicate_rows(p.rows, p.n, p.num_rows, s_rows, &s_lo, &s_hi);  // table_index; NULL: rows 0..n-1
+  // the pool is checked only for valid inputs, then the ids about to leave
+  // the list: free_pages[free_n - total, free_n)
+  const bool inputs_ok = block_or(err, &s_err) == 0;
+  const bool pool_ok = free_n >= 0 && free_n <= p.capacity && total <= free_n;
+  if (inputs_ok && !pool_ok && threadIdx.x == 0) err |= YL_DEVERR_POOL_EMPTY;
+  if (inputs_ok && pool_ok) {
     for (int64_t k = threadIdx.x; k < total; k += kPoolThreads)
       if (!page_ok(p.free_pages[free_n - total + k], p.capacity)) err |= YL_DEVERR_PAGE_RANGE;
   }
@@ -163,6 +220,8 @@ __global__ void __launch_bounds__(kPoolThreads) release_pages_kernel(const __gri
   __shared__ int64_t sums[32];
   __shared__ uint32_t s_err;
   __shared__ int64_t s_free;
+  __shared__ uint32_t s_rows[kRowBitmapWords];
+  __shared__ int32_t s_lo, s_hi;
   pdl_wait();
   if (threadIdx.x == 0) {
     s_err = 0;
@@ -186,7 +245,10 @@ __global__ void __launch_bounds__(kPoolThreads) release_pages_kernel(const __gri
     block_exclusive_scan(count, t, sums);
     total += t;
   }
-  if (threadIdx.x == 0 && (free_n < 0 || free_n + total > p.capacity)) err |= YL_DEVERR_POOL_OVERFLOW;
+  err |= duplicate_rows(p.rows, p.n, p.num_rows, s_rows, &s_lo, &s_hi);
+  // the free list is checked only for valid inputs
+  if (block_or(err, &s_err) == 0 && threadIdx.x == 0 && (free_n < 0 || free_n + total > p.capacity))
+    err |= YL_DEVERR_POOL_OVERFLOW;
   if (block_or(err, &s_err) != 0) {
     if (threadIdx.x == 0) raise_deverr(p.error_word, s_err);
     return;

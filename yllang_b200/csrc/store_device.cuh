@@ -52,6 +52,7 @@ struct StoreParams {
   uint32_t row_units;   // row_bytes / unit, generic kernel only
   FastDiv by_tokens;    // divides a row id by N
   SelfSlots self;
+  uint64_t wait_limit_ns;  // bulk-copy kernels: bound of the first wait for a round's rows
 };
 
 // ---------------------------------------------------------------------------

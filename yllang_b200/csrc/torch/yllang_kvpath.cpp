@@ -38,7 +38,8 @@ std::string DeviceErrorNames(uint32_t bits) {
       {YL_DEVERR_INDPTR_OVERFLOW, "INDPTR_OVERFLOW"}, {YL_DEVERR_TABLE_ROW, "TABLE_ROW"},
       {YL_DEVERR_TOKEN_COUNT, "TOKEN_COUNT"},         {YL_DEVERR_TIMEOUT, "TIMEOUT"},
       {YL_DEVERR_INDEX_RANGE, "INDEX_RANGE"},         {YL_DEVERR_POSITION_RANGE, "POSITION_RANGE"},
-      {YL_DEVERR_POOL_EMPTY, "POOL_EMPTY"},           {YL_DEVERR_POOL_OVERFLOW, "POOL_OVERFLOW"}};
+      {YL_DEVERR_POOL_EMPTY, "POOL_EMPTY"},           {YL_DEVERR_POOL_OVERFLOW, "POOL_OVERFLOW"},
+      {YL_DEVERR_DUPLICATE_ROW, "DUPLICATE_ROW"}};
   std::string out;
   for (const auto &[bit, name] : kNames) {
     if ((bits & bit) == 0) continue;

@@ -46,18 +46,24 @@ def _word(error_word: torch.Tensor | None, device: torch.device, what: str) -> i
 
 class _Errors:
     """The error word of one call: the caller's, or in debug mode a private
-    one that check() reads back after the launch."""
+    one that check() reads back after the launch.  The private word is zeroed
+    on the call's stream and read after that stream has finished, so a call
+    on a side stream is checked like one on the current stream."""
 
-    def __init__(self, error_word: torch.Tensor | None, device: torch.device, what: str):
+    def __init__(self, error_word: torch.Tensor | None, device: torch.device, what: str,
+                 stream: torch.cuda.Stream | None = None):
         self.what = what
         self.private = None
         self.tensor = error_word
         if error_word is None and CHECK_DEVICE_ERRORS:
-            self.private = self.tensor = torch.zeros(1, dtype=torch.int32, device=device)
+            self.stream = stream if stream is not None else torch.cuda.current_stream(device)
+            with torch.cuda.stream(self.stream):
+                self.private = self.tensor = torch.zeros(1, dtype=torch.int32, device=device)
         self.ptr = _word(self.tensor, device, what)
 
     def check(self) -> None:
         if self.private is not None:
+            self.stream.synchronize()
             bits = int(self.private.item()) & 0xFFFFFFFF
             if bits:
                 raise PanicError(f"{self.what}: device error bits {bits:#x} ({_abi.deverr_names(bits)})")
@@ -129,7 +135,7 @@ def store_kv_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_ca
     """
     if k.shape[-2] == 0:
         return
-    errs = _Errors(error_word, k.device, "store_kv_cache")
+    errs = _Errors(error_word, k.device, "store_kv_cache", stream)
     args = store_args(k, v, k_cache, v_cache, slots, errs.tensor)
     _abi.check(_abi.kv_store_raw(args, _stream(stream, k.device)))
     errs.check()
@@ -201,7 +207,7 @@ def build_index(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torc
                          torch.empty(B, **i32), torch.empty(B + 1, **i32),
                          torch.empty(slot_capacity, dtype=slot_dtype, device=dev))
     _check_out(out, B, dev)
-    errs = _Errors(error_word, dev, "build_index")
+    errs = _Errors(error_word, dev, "build_index", stream)
     a = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, errs.tensor)
     _abi.check(_abi.build_index_raw(a, _stream(stream, dev)))
     errs.check()
@@ -250,7 +256,7 @@ def kv_step(prior_len: torch.Tensor, new_len: torch.Tensor, page_table: torch.Te
     _check(out.slot_mapping.numel() >= N, f"out.slot_mapping holds {out.slot_mapping.numel()} < N={N} slots")
     a = _abi.StepArgs()
     a.store = store_args(k, v, k_cache, v_cache, out.slot_mapping[:N], None)
-    errs = _Errors(error_word, prior_len.device, "kv_step")  # the step reports store errors here too
+    errs = _Errors(error_word, prior_len.device, "kv_step", stream)  # the step reports store errors here too
     a.index = index_args(prior_len, new_len, page_table, page_size, table_index, num_pages, out, errs.tensor)
     _abi.check(_abi.kv_step_raw(a, _stream(stream, k.device)))
     errs.check()
@@ -284,7 +290,7 @@ def gather_rows(indices: torch.Tensor, table: torch.Tensor, out: torch.Tensor | 
     a.table_row_stride = table.stride(0) * item
     a.out_row_stride = out.stride(0) * item
     a.num_rows = table.shape[0]
-    errs = _Errors(error_word, table.device, "gather_rows")
+    errs = _Errors(error_word, table.device, "gather_rows", stream)
     a.error_word = errs.ptr
     _abi.check(_abi.gather_rows_raw(a, _stream(stream, table.device)))
     errs.check()
@@ -310,6 +316,8 @@ def make_2d_indices(ranges: torch.Tensor, out: torch.Tensor | None = None, count
     _check(ranges.is_contiguous(), "ranges must be contiguous")
     dev = ranges.device
     if out is None:
+        if stream is not None:
+            stream.synchronize()  # the ranges may come from work on the call's stream
         host = ranges.cpu()
         row, lo, hi = host[:, 0], host[:, 1], host[:, 2]
         _check(bool((row >= 0).all() and (lo >= 0).all() and (hi >= lo).all()),
@@ -318,7 +326,8 @@ def make_2d_indices(ranges: torch.Tensor, out: torch.Tensor | None = None, count
                "ranges: row + col_end passes INT64_MAX")
         total = sum((hi - lo).tolist())
         _check(total < (1 << 40), f"ranges: {total} indices is not below 2^40")
-        out = torch.empty(total, dtype=torch.int64, device=dev)
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream(dev)):
+            out = torch.empty(total, dtype=torch.int64, device=dev)  # owned by the stream that writes it
     _check(out.dtype == torch.int64 and out.dim() == 1 and out.is_contiguous() and out.device == dev,
            "out must be a contiguous int64 [capacity] tensor on the ranges' device")
     if count is not None:
@@ -330,7 +339,7 @@ def make_2d_indices(ranges: torch.Tensor, out: torch.Tensor | None = None, count
     a.count = count.data_ptr() if count is not None else None
     a.num_ranges = ranges.shape[0]
     a.indices_capacity = out.numel()
-    errs = _Errors(error_word, dev, "make_2d_indices")
+    errs = _Errors(error_word, dev, "make_2d_indices", stream)
     a.error_word = errs.ptr
     _abi.check(_abi.make_2d_indices_raw(a, _stream(stream, dev)))
     errs.check()
@@ -418,7 +427,7 @@ def qkv_norm_rope_store(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cac
     a.q_out_row_stride = q_out.stride(0) * item
     a.cache_row_stride = k_cache.stride(0) * item
     a.num_slots = k_cache.shape[0]
-    errs = _Errors(error_word, q.device, "qkv_norm_rope_store")
+    errs = _Errors(error_word, q.device, "qkv_norm_rope_store", stream)
     a.error_word = errs.ptr
     _abi.check(_abi.qkv_store_raw(a, _stream(stream, q.device)))
     errs.check()
@@ -470,7 +479,7 @@ class DevicePagePool:
         a.new_len = self._vec(new_len, B, "new_len")
         a.table_index = self._vec(table_index, B, "table_index") if table_index is not None else None
         a.page_size, a.batch_size = page_size, B
-        errs = _Errors(error_word, self.device, "DevicePagePool.reserve")
+        errs = _Errors(error_word, self.device, "DevicePagePool.reserve", stream)
         a.error_word = errs.ptr
         _abi.check(_abi.reserve_pages_raw(a, _stream(stream, self.device)))
         errs.check()
@@ -486,7 +495,7 @@ class DevicePagePool:
         a.rows = self._vec(rows, R, "rows")
         a.num_tokens = self._vec(num_tokens, R, "num_tokens")
         a.page_size, a.num_release = page_size, R
-        errs = _Errors(error_word, self.device, "DevicePagePool.release")
+        errs = _Errors(error_word, self.device, "DevicePagePool.release", stream)
         a.error_word = errs.ptr
         _abi.check(_abi.release_pages_raw(a, _stream(stream, self.device)))
         errs.check()

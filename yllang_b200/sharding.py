@@ -51,3 +51,17 @@ def sum_over_ranks(value: float, group=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
     return float(t.item())
+
+
+def gather_over_ranks(value: float, group=None) -> list[float]:
+    """`value` of every rank of the process group, in rank order ([value]
+    without an initialised group)."""
+    import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized():
+        return [value]
+    dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+    world = dist.get_world_size(group)
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t, group=group)
+    return [float(x.item()) for x in out]
