@@ -519,8 +519,8 @@ def host_step_setup(b: workloads.Batch, pool_gb: float = 4.0):
         E = hb.kv_heads * hb.head_dim
         rng = np.random.default_rng(r)
         n = hb.layers * hb.tokens * E
-        k = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
-        v = np.frombuffer(rng.bytes(2 * n), np.uint16).reshape(hb.layers, hb.tokens, E)
+        k = np.frombuffer(bytearray(rng.bytes(2 * n)), np.uint16).reshape(hb.layers, hb.tokens, E)
+        v = np.frombuffer(bytearray(rng.bytes(2 * n)), np.uint16).reshape(hb.layers, hb.tokens, E)
         sets.append((hb, k, v))
     hb = sets[0][0]
     pool = np.zeros((2, hb.layers, hb.num_pages * hb.page_size, hb.kv_heads * hb.head_dim), np.uint16)

@@ -26,29 +26,37 @@ import yllang_b200 as yl
 from yllang_b200 import workloads
 
 dev = torch.device("cuda:0")
-b = workloads.llama3_decode(num_pages=4096)  # 256 tokens x 32 layers x 2 KB rows
-L, E, S = b.layers, b.kv_heads * b.head_dim, b.num_pages * b.page_size
-t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
-prior, new, table = t(b.prior_len), t(b.new_len), t(b.page_table)
 g = torch.Generator(device=dev).manual_seed(0)
-k = torch.randn(L, b.tokens, E, generator=g, device=dev).to(torch.bfloat16)
-v = torch.randn(L, b.tokens, E, generator=g, device=dev).to(torch.bfloat16)
+t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
 i32 = dict(dtype=torch.int32, device=dev)
-out = yl.BatchIndex(torch.empty(b.batch + 1, **i32), torch.empty(b.total_pages, **i32), torch.empty(b.batch, **i32),
-                    torch.empty(b.batch + 1, **i32), torch.empty(b.tokens, dtype=torch.int64, device=dev))
-yl.build_index(prior, new, table, b.page_size, num_pages=b.num_pages, out=out)
-slots = out.slot_mapping.clone()
 
 
-def attempt(which):
-    pool = torch.empty(2, L, S, E, dtype=torch.bfloat16, device=dev)
+def case(batch):
+    # decode steps of 32 layers x 2 KB rows; at 1,024 sequences every CTA of
+    # the step's bulk-copy kernel stages its rows over several rounds, so some
+    # round's first wait starts while its copies are in flight
+    b = workloads.llama3_decode(num_pages=8192, batch=batch)
+    E = b.kv_heads * b.head_dim
+    k = torch.randn(b.layers, b.tokens, E, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(b.layers, b.tokens, E, generator=g, device=dev).to(torch.bfloat16)
+    out = yl.BatchIndex(torch.empty(b.batch + 1, **i32), torch.empty(b.total_pages, **i32),
+                        torch.empty(b.batch, **i32), torch.empty(b.batch + 1, **i32),
+                        torch.empty(b.tokens, dtype=torch.int64, device=dev))
+    lens = (t(b.prior_len), t(b.new_len), t(b.page_table))
+    yl.build_index(*lens, b.page_size, num_pages=b.num_pages, out=out)
+    return b, k, v, lens, out, out.slot_mapping.clone()
+
+
+def attempt(which, b, k, v, lens, out, slots):
+    L, S = b.layers, b.num_pages * b.page_size
+    pool = torch.empty(2, L, S, k.shape[-1], dtype=torch.bfloat16, device=dev)
     pool.view(torch.int16).random_(-2**15, 2**15, generator=g)
     orig = pool.clone()
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     if which == "store":
         yl.store_kv_cache(k, v, pool[0], pool[1], slots, error_word=err)
     else:
-        yl.kv_step(prior, new, table, b.page_size, k, v, pool[0], pool[1], out, num_pages=b.num_pages, error_word=err)
+        yl.kv_step(*lens, b.page_size, k, v, pool[0], pool[1], out, num_pages=b.num_pages, error_word=err)
     torch.cuda.synchronize()
     bits = int(err.item())
     assert bits & ~yl.DEVERR_TIMEOUT == 0, hex(bits)
@@ -66,13 +74,15 @@ def attempt(which):
     return bits, stored
 
 
-for which in ("store", "step"):
+for which, batch in (("store", 256), ("step", 1024)):
+    data = case(batch)
+    b = data[0]
     seen = False
     for _ in range(5):
-        bits, stored = attempt(which)
+        bits, stored = attempt(which, *data)
         if bits & yl.DEVERR_TIMEOUT:
             seen = True
-            assert stored < 2 * L * b.tokens
+            assert stored < 2 * b.layers * b.tokens
             break
     assert seen, f"{which}: no wait gave up in five tries"
     assert float(torch.ones(1000, device=dev).sum().item()) == 1000.0  # the context still runs work
@@ -81,6 +91,8 @@ print("bulk wait timeouts ok")
 
 
 def test_bulk_copy_waits_time_out_cleanly(cuda):
+    import torch
+    torch.cuda.empty_cache()  # the child allocates 35 GB
     env = dict(os.environ, YL_BULK_WAIT_LIMIT_NS="1", YL_STORE_ENGINE="tma", YL_STEP_MODE="tma")
     r = subprocess.run([sys.executable, "-c", CHILD], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

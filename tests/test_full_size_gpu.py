@@ -30,6 +30,16 @@ from yllang_b200 import workloads
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _release_device_memory():
+    """Hand the tens of GB these tests cache back to the device, so tests that
+    run a child process afterwards can allocate."""
+    yield
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
 def _dev(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
 

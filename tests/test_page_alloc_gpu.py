@@ -122,15 +122,15 @@ def test_duplicate_rows_change_nothing(cuda, case, spread):
         assert opool.reserve(otable, zeros, lens, ps, table_index=rows) == 0
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    dup = rows.copy()
-    dup[B - 3] = dup[5]  # far apart: first and last windows when spread
+    dup, dlens = rows.copy(), lens.copy()
+    dup[B - 3], dlens[B - 3] = dup[5], lens[5]  # far apart: first and last windows when spread
     free0, table0 = _state(pool, table)
     if case == "reserve":
         pool.reserve(table, t(zeros), t(lens), ps, table_index=t(dup), error_word=err)
         want = opool.reserve(otable, zeros, lens, ps, table_index=dup)
-    else:
-        pool.release(table, t(dup), t(lens), ps, error_word=err)
-        want = opool.release(otable, dup, lens, ps)
+    else:  # the repeated row releases the tokens it holds: nothing but the repeat is wrong
+        pool.release(table, t(dup), t(dlens), ps, error_word=err)
+        want = opool.release(otable, dup, dlens, ps)
     free, got = _state(pool, table)
     assert want == yl.DEVERR_DUPLICATE_ROW and int(err.item()) == want
     assert np.array_equal(free, free0) and np.array_equal(got, table0)
