@@ -163,10 +163,12 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # workload set-up
 # ---------------------------------------------------------------------------
-def make_batches(name: str, world: int, pool_bytes: int, rotate: int):
-    """R batches of one workload for this rank (same lengths, different pages)."""
+def make_batches(name: str, world: int, pool_bytes: int, rotate: int, whole_job: bool = False):
+    """R batches of one workload for this rank (same lengths, different pages).
+    whole_job: the batch of all `world` ranks with every KV head (what one
+    host runs when it does the whole job's work)."""
     h0, h1 = sharding.head_range(0, world, 8)  # raises unless the 8 KV heads split evenly
-    heads = h1 - h0
+    heads = 8 if whole_job else h1 - h0
     if name == "llama3_decode":
         layers, ps, row = 32, 16, heads * 128 * 2
         P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
@@ -181,7 +183,7 @@ def make_batches(name: str, world: int, pool_bytes: int, rotate: int):
     elif name == "qwen72b_decode":
         layers, ps, row = 80, 16, heads * 128 * 2
         P = workloads.pool_pages_for(pool_bytes, layers, row, ps)
-        mk = lambda r: workloads.qwen72b_decode(P, tp=world, batch=512, seed_pages=2 + r)
+        mk = lambda r: workloads.qwen72b_decode(P, tp=8 // heads, batch=512, seed_pages=2 + r)
         desc = {"workload": "qwen2_72b_tp_decode", "model_shape": "Qwen2-72B", "global_batch": 512,
                 "scaling": "strong"}
     elif name.startswith("mixed"):
@@ -683,7 +685,8 @@ def run_reference(args, world, rank):
     helper and the reference's own GPU store kernel."""
     if rank != 0:
         return
-    batches, desc = make_batches(args.workload, 1, 150e9, 1)
+    # the whole job of our arm at this world size: its global batch, every KV head
+    batches, desc = make_batches(args.workload, world, 150e9, 1, whole_job=True)
     b = batches[0]
     torch.set_num_threads(os.cpu_count() or 1)
     threads = torch.get_num_threads()
@@ -740,7 +743,9 @@ def run_reference(args, world, rank):
 
 def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
-    shape_world = 1 if args.replicas else world  # replicas: every rank runs the one-GPU shapes
+    # replicas: every rank runs the one-GPU shapes; --shape-ranks M: one rank of
+    # an M-GPU run's shapes on each GPU (a one-GPU view of a rank's work)
+    shape_world = 1 if args.replicas else (args.shape_ranks or world)
     peak, peak_kind = load_peaks()
     wl = Workload(args.workload, args, shape_world, dev, rank)
     desc = dict(wl.desc)
@@ -789,7 +794,8 @@ def run_ours(args, world, rank, local):
         "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded lengths and fragmented page tables, K/V N(0,1) cast to bf16",
         "config": dict(desc, parallelism=(f"replicas x{world}" if args.replicas else f"kv-head shard x{world}")
-                       if world > 1 else "single GPU",
+                       if world > 1 else ("single GPU" if shape_world == 1
+                                          else f"one rank of a kv-head shard x{shape_world}, alone"),
                        path=(f"yl_kv_step ({os.environ.get('YL_STEP_MODE', 'pdl')})" if wl.fused
                              else "build_index + store_kv_cache"),
                        l2=f"inputs rotate over {wl.R} sets ({wl.R * wl.per_set / 1e6:.0f} MB > 2 x L2), "
@@ -1145,6 +1151,8 @@ def main():
     ap.add_argument("--no-make2d", action="store_true", help="skip the range-expansion (Make2DIndices) line")
     ap.add_argument("--replicas", action="store_true",
                     help="every rank runs the full-head one-GPU workload (a sanity check of the head-sharded run)")
+    ap.add_argument("--shape-ranks", type=int, default=0,
+                    help="run one rank's shapes of a kv-head shard over this many GPUs (0: the real world size)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -192,11 +192,16 @@ int launch_index(const IndexParams &p, cudaStream_t stream) {
   // so big batches use 1024-thread blocks (4x fewer scans), at most one per SM.
   const int64_t work = p.indices_cap + p.slots_cap;
   const int64_t sms = sm_count();
+  // A fill of more than two elements per thread of a full 256-thread grid
+  // (long contexts: Qwen2-72B decode, 512 sequences of ~1,000 pages) takes the
+  // big-batch kernels too, whose fill keeps several page-table loads in flight
+  // per thread instead of one.
+  const bool heavy = p.batch > kBigBatch || work > 2 * 4 * sms * kIndexThreads;
   // beside a store (a decode step whose store computes its own slots): the
   // 256-thread kernel at two blocks per SM at most, so two of the store's
-  // CTAs fit beside them, with the big-batch staging and fill above 512
-  const bool big = p.batch > kBigBatch && !p.beside_store;
-  const bool big_narrow = p.batch > kBigBatch && p.beside_store;
+  // CTAs fit beside them, with the big-batch staging and fill
+  const bool big = heavy && !p.beside_store;
+  const bool big_narrow = heavy && p.beside_store;
   const int threads = big ? kIndexThreadsBig : kIndexThreads;
   // (beside the store: one block per SM above 1,024 sequences, measured 0.5 us
   // faster at 2,048; two up to 1,024, where one block per SM measured 0.4-2 us slower)
