@@ -4,7 +4,7 @@ and through the two separate calls:
 
 * Llama-3-8B decode: 256 sequences, 32 layers, 2 KB rows; and the per-rank
   shapes of its head-sharded runs (512 / 1,024 / 2,048 sequences at 4 / 2 / 1
-  KV heads), which take the slot-cache and token-major store kernels;
+  KV heads, 1,024- to 256-byte rows);
 * ragged prefill: 64 prompts U[128, 4096] (~131 k tokens), 32 layers;
 * Qwen2-72B decode: 512 sequences, 80 layers, at 8 / 4 / 2 / 1 KV heads per
   GPU (2,048- to 256-byte rows);

@@ -170,8 +170,8 @@ def test_step_other_modes(cuda, mode):
 @pytest.mark.parametrize("tix,slot_dtype", [(False, torch.int64), (True, torch.int64), (False, torch.int32)])
 def test_step_decode_batch_slot_rules(cuda, B, tix, slot_dtype):
     """Decode batches (one new token per sequence), where the store computes
-    its own slots beside the index build (per row at 200 sequences, cached
-    per CTA at 300, token-major at 1,500): page ids outside the pool, a row
+    its own slots beside the index build (one slot per lane group and token,
+    at 200, 300 and 1,500 sequences): page ids outside the pool, a row
     outside the table, a sequence past its row's pages, a negative prior
     length and an int32 slot overflow must give the slots, pool and error
     bits the oracle gives."""

@@ -45,7 +45,7 @@ struct IndexParams {
 constexpr int kScanScratch = 67;
 constexpr int kScanMaxWord = 66;
 
-// Largest page count of any sequence, after scan_batch<true>.
+// Largest page count of any sequence, after scan_batch.
 __device__ __forceinline__ int32_t scanned_max_pages(const int64_t *scratch) {
   return reinterpret_cast<const int32_t *>(scratch)[2 * kScanMaxWord];
 }
@@ -96,35 +96,33 @@ __device__ __forceinline__ SeqFacts seq_facts(const IndexParams &p, int i, bool 
 // Sequences staged per thread per round of the scan (their loads in flight together).
 constexpr int kStageUnroll = 8;
 
-// Phase A: scan page and token counts of all sequences into kvp[0..B] and
-// qop[0..B] (shared or global memory).  The counts are first staged in
-// kvp/qop (coalesced); each warp then scans its contiguous segment 32 entries
-// at a time with shuffles (conflict-free), the warp totals are scanned once,
-// and each warp adds its offset.  Returns false (uniformly across the block)
-// when a sum passes INT32_MAX; the fill must then be skipped.
-// kBig (the big-batch kernels): the counts are staged kStageUnroll
-// sequences per thread per round with their loads in flight together, and
-// the batch's largest page count is kept for the fill's choice; otherwise one
-// sequence per thread per pass (small batches: at most a pass or two).
+// Phase A: page and token counts of all sequences, exclusive-scanned into
+// kvp[0..B] and qop[0..B] (shared or global memory).  Thread k owns the
+// consecutive sequences [k m, k m + m), m = ceil(B / threads): it loads their
+// lengths kStageUnroll at a time (the loads in flight together), writes their
+// counts and keeps their sums; then one warp scan of the thread sums, one
+// scan of the warp sums, and a second pass over its own sequences turns the
+// counts into offsets.  A block scans B sequences with one shuffle scan per
+// warp whatever B is (a scan 32 entries at a time costs a shuffle scan per 32
+// sequences, which at a few thousand sequences dominated the kernel).
+// Returns false (uniformly across the block) when a total passes INT32_MAX;
+// the fill must then be skipped.  The batch's largest page count is left in
+// scratch for the fill's choice (scanned_max_pages).
 template <bool kBig = false>
 __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *qop, int64_t *scratch, bool report) {
   const int B = p.batch;
-  if constexpr (!kBig) {
-    for (int i = threadIdx.x; i < B; i += blockDim.x) {
-      const SeqFacts f = seq_facts(p, i, report);
-      kvp[i] = f.pages;
-      qop[i] = f.fresh;
-    }
-    __syncthreads();
-  } else {
+  const int m = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+  const int s0 = min(B, static_cast<int>(threadIdx.x) * m), s1 = min(B, s0 + m);
+  int32_t *max_word = reinterpret_cast<int32_t *>(scratch) + 2 * kScanMaxWord;
+  if (threadIdx.x == 0) *max_word = 0;
+  int64_t sa = 0, sb = 0;
   int32_t max_pages = 0;
-  if (threadIdx.x == 0) reinterpret_cast<int32_t *>(scratch)[2 * kScanMaxWord] = 0;
-  for (int base = threadIdx.x; base < B; base += kStageUnroll * blockDim.x) {
+  for (int base = s0; base < s1; base += kStageUnroll) {
     int32_t pl[kStageUnroll], nl[kStageUnroll], rw[kStageUnroll];
 #pragma unroll
     for (int u = 0; u < kStageUnroll; ++u) {
-      const int i = base + u * static_cast<int>(blockDim.x);
-      if (i < B) {
+      const int i = base + u;
+      if (i < s1) {
         pl[u] = __ldg(p.prior_len + i);
         nl[u] = __ldg(p.new_len + i);
         rw[u] = p.table_index != nullptr ? __ldg(p.table_index + i) : i;
@@ -132,71 +130,57 @@ __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *q
     }
 #pragma unroll
     for (int u = 0; u < kStageUnroll; ++u) {
-      const int i = base + u * static_cast<int>(blockDim.x);
-      if (i < B) {
+      const int i = base + u;
+      if (i < s1) {
         const SeqFacts f = facts_of(p, pl[u], nl[u], rw[u], report);
         kvp[i] = f.pages;
         qop[i] = f.fresh;
+        sa += f.pages;
+        sb += f.fresh;
         max_pages = max(max_pages, f.pages);
       }
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) max_pages = max(max_pages, __shfl_xor_sync(0xffffffffu, max_pages, o));
-  __syncthreads();  // the max word's reset is visible before any update
-  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int32_t *>(scratch) + 2 * kScanMaxWord, max_pages);
-  __syncthreads();
-  }
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
-  const int seg = (((B + nwarps - 1) / nwarps) + 31) & ~31;
-  const int s0 = min(B, warp * seg), s1 = min(B, s0 + seg);
-  int64_t ca = 0, cb = 0;  // running totals of this warp's segment
-  for (int base = s0; base < s1; base += 32) {
-    const int i = base + lane;
-    const int64_t x = i < s1 ? kvp[i] : 0, y = i < s1 ? qop[i] : 0;
-    int64_t a = x, b = y;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  int64_t a = sa, b = sb;  // inclusive scan of the thread sums within the warp
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t ua = __shfl_up_sync(0xffffffffu, a, o);
-      const int64_t ub = __shfl_up_sync(0xffffffffu, b, o);
-      if (lane >= o) {
-        a += ua;
-        b += ub;
-      }
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t ua = __shfl_up_sync(0xffffffffu, a, o);
+    const int64_t ub = __shfl_up_sync(0xffffffffu, b, o);
+    if (lane >= o) {
+      a += ua;
+      b += ub;
     }
-    // exclusive within the segment; int32 wrap here is harmless, the totals
-    // are checked below before any offset is used
-    if (i < s1) {
-      kvp[i] = static_cast<int32_t>(ca + a - x);
-      qop[i] = static_cast<int32_t>(cb + b - y);
-    }
-    ca += __shfl_sync(0xffffffffu, a, 31);
-    cb += __shfl_sync(0xffffffffu, b, 31);
   }
-  if (lane == 0) {
-    scratch[warp] = ca;
-    scratch[32 + warp] = cb;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) max_pages = max(max_pages, __shfl_xor_sync(0xffffffffu, max_pages, o));
+  if (lane == 31) {
+    scratch[warp] = a;
+    scratch[32 + warp] = b;
   }
-  __syncthreads();
+  __syncthreads();  // warp sums, and the max word's reset, visible
+  if (lane == 0) atomicMax(max_word, max_pages);
   if (warp == 0) {
-    int64_t a = lane < nwarps ? scratch[lane] : 0, b = lane < nwarps ? scratch[32 + lane] : 0;
-    const int64_t a0 = a, b0 = b;
+    int64_t wa = lane < nwarps ? scratch[lane] : 0, wb = lane < nwarps ? scratch[32 + lane] : 0;
+    const int64_t wa0 = wa, wb0 = wb;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int64_t ua = __shfl_up_sync(0xffffffffu, a, o);
-      const int64_t ub = __shfl_up_sync(0xffffffffu, b, o);
+      const int64_t ua = __shfl_up_sync(0xffffffffu, wa, o);
+      const int64_t ub = __shfl_up_sync(0xffffffffu, wb, o);
       if (lane >= o) {
-        a += ua;
-        b += ub;
+        wa += ua;
+        wb += ub;
       }
     }
-    scratch[lane] = a - a0;  // exclusive warp offsets
-    scratch[32 + lane] = b - b0;
+    if (lane < nwarps) {
+      scratch[lane] = wa - wa0;  // exclusive warp offsets
+      scratch[32 + lane] = wb - wb0;
+    }
     if (lane == 31) {
-      scratch[64] = a;  // block totals
-      scratch[65] = b;
+      scratch[64] = wa;  // block totals
+      scratch[65] = wb;
     }
   }
   __syncthreads();
@@ -205,10 +189,14 @@ __device__ inline bool scan_batch(const IndexParams &p, int32_t *kvp, int32_t *q
     if (report && threadIdx.x == 0) raise_deverr(p.error_word, YL_DEVERR_INDPTR_OVERFLOW);
     return false;
   }
-  const int32_t oa = static_cast<int32_t>(scratch[warp]), ob = static_cast<int32_t>(scratch[32 + warp]);
-  for (int i = s0 + lane; i < s1; i += 32) {
-    kvp[i] += oa;
-    qop[i] += ob;
+  // every prefix is at most its total, so the offsets fit in int32
+  int32_t oa = static_cast<int32_t>(scratch[warp] + a - sa), ob = static_cast<int32_t>(scratch[32 + warp] + b - sb);
+  for (int i = s0; i < s1; ++i) {
+    const int32_t ca = kvp[i], cb = qop[i];
+    kvp[i] = oa;
+    qop[i] = ob;
+    oa += ca;
+    ob += cb;
   }
   if (threadIdx.x == 0) {
     kvp[B] = static_cast<int32_t>(ta);

@@ -200,11 +200,8 @@ static size_t step_smem(int batch) { return kScanScratch * sizeof(int64_t) + 2 *
 enum class StepMode { kPdl, kTma, kFused, kSerial };
 
 // Decode batches up to kStepSelfSlotsBatch sequences have the store compute
-// their slots: per row up to kStepSlotCacheFrom, then once per CTA into
-// shared memory, and above kStepTokenMajorFrom with the token-major store.
+// their slots (store_decode_kernel: one slot per lane group and token).
 constexpr int kStepSelfSlotsBatch = 16384;
-constexpr int kStepSlotCacheFrom = 256;
-constexpr int kStepTokenMajorFrom = 512;
 static StepMode step_mode() {
   static const StepMode m = [] {
     const char *e = std::getenv("YL_STEP_MODE");
@@ -311,18 +308,14 @@ extern "C" int yl_kv_step(const yl_step_args *a, cudaStream_t stream) {
     // K/V loads overlap the index build and only the slot reads wait for it.
     // A decode batch (N == B, and the store checks every new_len is 1) lets
     // the store compute its slots itself and run beside the index build
-    // instead of after it; the index build then runs as 256-thread blocks,
-    // two per SM at most, to leave the store room.  Measured per step (one
-    // B200, 32 layers): B = 256 15.1 -> 13.7 us with a slot computed per row
-    // (14.1 with a per-CTA slot cache); B = 512 18.2 -> 16.4 us with the
-    // cache (18.0 per row).  Above 512 the plane-major store would have every
-    // CTA compute every slot (B = 2,048: 23.0 -> 28.8 us), so it runs
-    // token-major, each CTA computing only its own tokens' slots.
+    // instead of after it: store_decode_kernel gives each lane group one
+    // token, whose slot it computes once, and a run of that token's layers,
+    // which it walks by the layer strides.  The index build then runs as
+    // 256-thread blocks, at most two per SM, to leave the store room.
     if (step_mode() == StepMode::kPdl && s.num_tokens == ix.batch && ix.batch <= kStepSelfSlotsBatch) {
-      const int mode = ix.batch > kStepTokenMajorFrom ? 2 : (ix.batch > kStepSlotCacheFrom ? 1 : 0);
       sp.p.self = SelfSlots{ix.prior_len, ix.new_len, ix.page_table, ix.table_index, ix.page_table_stride,
                             ix.num_pages, ix.batch, ix.page_size, ix.max_pages_per_row, ix.num_table_rows,
-                            ix.slot64, mode, ix.by_page};
+                            ix.slot64, ix.by_page};
       ix.beside_store = 1;
     }
     rc = launch_index(ix, stream);

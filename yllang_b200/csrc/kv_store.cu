@@ -59,94 +59,65 @@ __global__ void __launch_bounds__(256) store_rows_kernel(const __grid_constant__
   }
 }
 
-// A decode step's store (see yl_kv_step): when every sequence adds one token
-// the kernel computes its slots itself — per row, or with kCached once per
-// CTA into shared memory — and does not wait for the index build; otherwise
-// it waits and reads the slots as store_rows_kernel does.  Separate kernels,
-// so the plain store keeps its own code and registers.
-template <int W, int G, int VPL, int R, typename SlotT, bool kCached>
-__global__ void __launch_bounds__(256) store_rows_self_kernel(const __grid_constant__ StoreParams p) {
-  extern __shared__ int64_t slot_cache[];
-  const uint32_t lane = threadIdx.x % G;
-  const uint32_t group = (blockIdx.x * blockDim.x + threadIdx.x) / G;
-  const uint32_t num_groups = (gridDim.x * blockDim.x) / G;
-
-  uint32_t base = group * R;
-  RowBatch<W, G, VPL, R> b;
-  b.load(p, base, lane);
-  const bool self = decode_batch(p.self);
-  if (!self) pdl_wait();
-  else if (kCached) fill_slot_cache(p.self, slot_cache, p.error_word);  // uniform per block
-  while (base < p.total_rows) {
-    int64_t slot[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-      slot[r] = !b.live[r] ? -1
-                : !self    ? load_slot<SlotT>(p.slots, b.token[r])
-                : kCached  ? slot_cache[b.token[r]]
-                           : decode_slot(p.self, b.token[r], p.error_word);
-#pragma unroll
-    for (int r = 0; r < R; ++r) b.resolve(p, r, slot[r]);
-    b.store(lane);
-    base += num_groups * R;
-    if (base < p.total_rows) b.load(p, base, lane);
-  }
-}
-
-// A big decode step's store: CTA c owns tokens [c T, c T + T) across every
-// plane (token-major), so it computes those T slots once (shared memory) and
-// reuses them for all 2L planes — with the plane-major order each token's
-// rows land in 2L different CTAs, each of which would compute its slot.  The
-// K/V reads stay contiguous within a plane.  Not a decode batch: it waits for
-// the index build and reads the slots, over the same rows.
-constexpr uint32_t kTokenMajorMaxTokens = 64;
+// A decode step's store, token by token.  Work unit u = (plane chunk c,
+// token t), u = c * N + t, one unit per lane group: the group computes its
+// token's slot once (or reads it, for a batch that is not a decode batch),
+// then copies the token's rows of planes [c * chunk, (c + 1) * chunk), R
+// planes in flight at a time, stepping its source and destination rows by the
+// layer strides (no per-row division or slot lookup, which for small rows
+// costs more issue slots than the copy).  Consecutive groups take consecutive
+// tokens of the same planes, so the K/V reads of a warp are contiguous.
 template <int W, int G, int VPL, int R, typename SlotT>
-__global__ void __launch_bounds__(256) store_tokens_self_kernel(const __grid_constant__ StoreParams p, uint32_t tpc) {
-  __shared__ int64_t s_slot[kTokenMajorMaxTokens];
+__global__ void __launch_bounds__(256) store_decode_kernel(const __grid_constant__ StoreParams p, uint32_t chunk,
+                                                           uint32_t planes) {
   const uint32_t lane = threadIdx.x % G;
-  const uint32_t lgroup = threadIdx.x / G;
-  const uint32_t step = (blockDim.x / G) * R;
+  const uint32_t unit = (blockIdx.x * blockDim.x + threadIdx.x) / G;
   const uint32_t N = p.by_tokens.d;
-  const uint32_t planes = p.total_rows / N;
-  const uint32_t t0 = blockIdx.x * tpc;
-  const uint32_t nt = t0 < N ? min(tpc, N - t0) : 0;
-  const uint32_t work = planes * nt;  // local row q: plane q / nt, token t0 + q % nt
-
-  RowBatch<W, G, VPL, R> b;
-  uint32_t rows[R];
-  bool ok[R];
-  auto pick = [&](uint32_t base) {
+  const uint32_t c = p.by_tokens.div(unit);
+  const uint32_t t = unit - c * N;
+  uint32_t pl = c * chunk;
+  const uint32_t end = min(pl + chunk, planes);
+  const char *src_k = p.k + static_cast<int64_t>(t) * p.k_row_stride;
+  const char *src_v = p.v + static_cast<int64_t>(t) * p.v_row_stride;
+  Vec<W> data[R][VPL];
+  auto load = [&](uint32_t first) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const uint32_t q = base + r;
-      ok[r] = q < work;
-      const uint32_t plane = ok[r] ? q / nt : 0;
-      rows[r] = plane * N + t0 + (q - plane * nt);
+      const uint32_t q = first + r;
+      if (q < end) {
+        const int64_t layer = q >> 1;
+        const char *src = (q & 1u) ? src_v + layer * p.v_layer_stride : src_k + layer * p.k_layer_stride;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) load_vec(data[r][j], src + (j * G + lane) * W);
+      }
     }
   };
-  uint32_t base = lgroup * R;
-  pick(base);
-  b.load_list(p, rows, ok, lane);
-  const bool self = decode_batch(p.self);
-  if (self) {
-    if (threadIdx.x < nt) s_slot[threadIdx.x] = decode_slot(p.self, t0 + threadIdx.x, p.error_word);
-    __syncthreads();  // uniform: self is the same on every thread
-  } else {
+  load(pl);
+  const bool self = decode_batch(p.self);  // block-uniform
+  int64_t slot = -1;
+  if (!self) {
     pdl_wait();
+    if (pl < end) slot = load_slot<SlotT>(p.slots, t);
+  } else if (pl < end) {
+    slot = decode_slot(p.self, t, p.error_word);
   }
-  while (base < work) {
-    int64_t slot[R];
+  const bool ok = pl < end && slot_ok(slot, p);
+  char *dst_k = p.k_cache + slot * p.cache_row_stride;
+  char *dst_v = p.v_cache + slot * p.cache_row_stride;
+  while (pl < end) {
+    if (ok) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-      slot[r] = !b.live[r] ? -1 : self ? s_slot[b.token[r] - t0] : load_slot<SlotT>(p.slots, b.token[r]);
+      for (int r = 0; r < R; ++r) {
+        const uint32_t q = pl + r;
+        if (q < end) {
+          char *dst = ((q & 1u) ? dst_v : dst_k) + static_cast<int64_t>(q >> 1) * p.cache_layer_stride;
 #pragma unroll
-    for (int r = 0; r < R; ++r) b.resolve(p, r, slot[r]);
-    b.store(lane);
-    base += step;
-    if (base < work) {
-      pick(base);
-      b.load_list(p, rows, ok, lane);
+          for (int j = 0; j < VPL; ++j) store_vec(dst + (j * G + lane) * W, data[r][j]);
+        }
+      }
     }
+    pl += R;
+    if (pl < end) load(pl);
   }
 }
 
@@ -275,12 +246,12 @@ __global__ void __launch_bounds__(256) store_rows_generic_kernel(const __grid_co
 // ---------------------------------------------------------------------------
 using StoreKernel = void (*)(StoreParams);
 
-using TokenKernel = void (*)(StoreParams, uint32_t);
+using DecodeKernel = void (*)(StoreParams, uint32_t, uint32_t);
 struct StoreVariant {
   StoreKernel fn;
   int group;  // lanes per row
   int rows;   // rows per group-iteration
-  TokenKernel tok = nullptr;  // the token-major kernel (fn unused)
+  DecodeKernel dec = nullptr;  // the decode step's token-by-token kernel (fn unused)
 };
 
 int fast_vector_bytes() {
@@ -291,23 +262,15 @@ int fast_vector_bytes() {
   return w;
 }
 
-// self: 0 the plain store, 1 the decode step's store computing slots per
-// row, 2 the same with the per-CTA slot cache, 3 the token-major store.
-static bool pick_fast(int64_t row_bytes, int w, bool slot64, int self, StoreVariant &out) {
+// self: the decode step's token-by-token store (store_decode_kernel), else
+// the plain store.
+static bool pick_fast(int64_t row_bytes, int w, bool slot64, bool self, StoreVariant &out) {
   return dispatch_row_shape(row_bytes, w, [&](auto shape) {
     using S = decltype(shape);
-    if (self == 1)
-      out = StoreVariant{slot64 ? store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int64_t, false>
-                                : store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int32_t, false>,
-                         S::G, S::R};
-    else if (self == 2)
-      out = StoreVariant{slot64 ? store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int64_t, true>
-                                : store_rows_self_kernel<S::W, S::G, S::VPL, S::R, int32_t, true>,
-                         S::G, S::R};
-    else if (self == 3)  // at most 4 rows per group (fewer registers: room beside the index build)
-      out = StoreVariant{nullptr, S::G, S::R > 4 ? 4 : S::R,
-                         slot64 ? store_tokens_self_kernel<S::W, S::G, S::VPL, (S::R > 4 ? 4 : S::R), int64_t>
-                                : store_tokens_self_kernel<S::W, S::G, S::VPL, (S::R > 4 ? 4 : S::R), int32_t>};
+    if (self)
+      out = StoreVariant{nullptr, S::G, S::R,
+                         slot64 ? store_decode_kernel<S::W, S::G, S::VPL, S::R, int64_t>
+                                : store_decode_kernel<S::W, S::G, S::VPL, S::R, int32_t>};
     else
       out = StoreVariant{slot64 ? store_rows_kernel<S::W, S::G, S::VPL, S::R, int64_t>
                                 : store_rows_kernel<S::W, S::G, S::VPL, S::R, int32_t>,
@@ -478,19 +441,26 @@ int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStre
   StoreVariant var{};
   bool fast = false;
   const int w = fast_vector_bytes();
-  const int self = plan.p.self.batch > 0 ? 1 + plan.p.self.cached : 0;
+  const bool self = plan.p.self.batch > 0;
   if (plan.unit == 16 && w == 32 && (plan.bits & 31u) == 0) fast = pick_fast(row_bytes, 32, slot64, self, var);
   if (!fast && plan.unit == 16) fast = pick_fast(row_bytes, 16, slot64, self, var);
-  if (!fast) var = pick_generic(plan.unit, slot64);
+  if (!fast) var = pick_generic(plan.unit, slot64);  // reads the slots after the index build (pdl_wait)
   const uint64_t rows_per_block = static_cast<uint64_t>(kStoreThreads / var.group) * var.rows;
   const uint64_t want = (plan.p.total_rows + rows_per_block - 1) / rows_per_block;
-  if (var.tok != nullptr) {
-    // token-major: T tokens per CTA, as few as the resident CTAs allow
+  if (var.dec != nullptr) {
+    // units of (plane chunk, token): chunks of R-plane multiples sized so
+    // that the resident lane groups of one wave take every unit
     const uint64_t n = plan.p.by_tokens.d;
-    const uint64_t ctas = static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.tok), 0);
-    uint64_t tpc = (n + (ctas < n ? ctas : n) - 1) / (ctas < n ? ctas : n);
-    if (tpc > kTokenMajorMaxTokens) tpc = kTokenMajorMaxTokens;  // the host caps the batch so this does not bind
-    const unsigned grid = static_cast<unsigned>((n + tpc - 1) / tpc);
+    const uint64_t planes = plan.p.total_rows / n;
+    const uint64_t groups = kStoreThreads / var.group;
+    const uint64_t R = static_cast<uint64_t>(var.rows);
+    const uint64_t resident = static_cast<uint64_t>(sm_count()) *
+                              blocks_per_sm(reinterpret_cast<const void *>(var.dec), 0) * groups;
+    uint64_t chunk = R * ((planes * n + resident * R - 1) / (resident * R));
+    const uint64_t max_chunk = (planes + R - 1) / R * R;
+    if (chunk > max_chunk) chunk = max_chunk;
+    const uint64_t units = (planes + chunk - 1) / chunk * n;
+    const unsigned grid = static_cast<unsigned>((units + groups - 1) / groups);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kStoreThreads);
@@ -501,7 +471,8 @@ int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStre
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, var.tok, plan.p, static_cast<uint32_t>(tpc));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, var.dec, plan.p, static_cast<uint32_t>(chunk),
+                                             static_cast<uint32_t>(planes));
     if (e != cudaSuccess) {
       cudaGetLastError();
       set_last_error(std::string("yl_kv_store launch: ") + cudaGetErrorString(e));
@@ -509,8 +480,7 @@ int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStre
     }
     return YL_OK;
   }
-  // the slot cache of a decode step's store
-  const size_t smem = fast && plan.p.self.cached == 1 ? static_cast<size_t>(plan.p.self.batch) * sizeof(int64_t) : 0;
+  const size_t smem = 0;
   const uint64_t cap =
       static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(var.fn), smem);
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);

@@ -29,8 +29,6 @@ struct SelfSlots {
   int32_t max_pages_per_row;
   int32_t num_table_rows;
   int32_t slot64;
-  int32_t cached;  // 0: a slot per row; 1: all `batch` slots once per CTA into shared memory (batch x 8
-                   // bytes); 2: the token-major kernel, each CTA its own tokens' slots
   FastDiv by_page;
 };
 
@@ -131,25 +129,6 @@ __device__ __forceinline__ int64_t decode_slot(const SelfSlots &s, uint32_t t, u
   if (in_range && (s.slot64 || slot <= INT_MAX)) return slot;
   raise_deverr(error_word, YL_DEVERR_PAGE_RANGE);
   return -1;
-}
-
-// Every token's slot of a decode batch into shared memory, four tokens per
-// thread per round with their loads in flight together.
-__device__ inline void fill_slot_cache(const SelfSlots &s, int64_t *cache, uint32_t *error_word) {
-  for (int t0 = threadIdx.x; t0 < s.batch; t0 += 4 * blockDim.x) {
-    int64_t v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + u * static_cast<int>(blockDim.x);
-      v[u] = t < s.batch ? decode_slot(s, static_cast<uint32_t>(t), error_word) : -1;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + u * static_cast<int>(blockDim.x);
-      if (t < s.batch) cache[t] = v[u];
-    }
-  }
-  __syncthreads();
 }
 
 template <typename SlotT>
