@@ -2,9 +2,12 @@
 
 * libyl_kvpath.so — the C-ABI CUDA library (kernels + yl_* entry points),
   compiled by nvcc for sm_100a only; depends on the CUDA runtime, not torch.
+* libyl_attention.so — flashinfer's paged decode / causal prefill kernels
+  (third-party, compiled from the headers flashinfer ships) behind a
+  torch-free interface, for the front end's Attention layer.
 * _C*.so — the C++17 libtorch front end (yllang::StoreKVCache, MHAKVCache,
-  the batch index builder and page allocator) as a Python extension linked
-  against libtorch and libyl_kvpath.so.
+  the batch index builder, page allocator and Attention) as a Python
+  extension linked against libtorch, libyl_kvpath.so and libyl_attention.so.
 
 Both land inside the package directory so that they travel with the source
 tree and are the files a process loads.
@@ -57,6 +60,39 @@ def build_library(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+ATTN_LIB = os.path.join(PKG, "libyl_attention.so")
+
+
+def _flashinfer_data() -> str:
+    """Source headers shipped inside the installed flashinfer package (its
+    own include tree, and the CCCL / CUTLASS trees it vendors)."""
+    import importlib.util
+    spec = importlib.util.find_spec("flashinfer")
+    if spec is None or spec.origin is None:
+        raise RuntimeError("flashinfer is not installed: the attention layer compiles its kernels from its headers")
+    return os.path.join(os.path.dirname(spec.origin), "data")
+
+
+def build_attention(force: bool = False, verbose: bool = False) -> str:
+    """nvcc-compile libyl_attention.so: flashinfer's paged decode and causal
+    paged prefill kernels for sm_100a behind csrc/torch/attention_fi.h (no
+    torch dependency; used by the front end's Attention)."""
+    src = os.path.join(CSRC, "torch", "attention_fi.cu")
+    deps = [src, os.path.join(CSRC, "torch", "attention_fi.h")]
+    if not force and not _stale(ATTN_LIB, deps):
+        return ATTN_LIB
+    fi = _flashinfer_data()
+    tmp = ATTN_LIB + ".tmp"
+    cmd = [_nvcc(), "-std=c++17", "-O3", *GENCODE, "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler",
+           "-fPIC,-fvisibility=hidden", "-shared", f"-I{fi}/cccl/libcudacxx/include", f"-I{fi}/include",
+           f"-I{fi}/cutlass/include", f"-I{fi}/spdlog/include", "-diag-suppress=20012,177,550", src, "-o", tmp]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, ATTN_LIB)
+    return ATTN_LIB
+
+
 def _ext_path() -> str:
     import sysconfig
     return os.path.join(PKG, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
@@ -74,7 +110,8 @@ def build_extension(force: bool = False, verbose: bool = False) -> str:
     tdir = os.path.join(CSRC, "torch")
     srcs = sorted(glob.glob(os.path.join(tdir, "*.cpp")))
     deps = srcs + glob.glob(os.path.join(tdir, "*.h")) + [os.path.join(INCLUDE, "yl_kvpath.h")]
-    if not force and not _stale(out, deps):
+    attn = build_attention(force=force, verbose=verbose)
+    if not force and not _stale(out, deps + [attn]):
         return out
     build_dir = os.path.join(PKG, "_build")
     os.makedirs(build_dir, exist_ok=True)
@@ -96,7 +133,7 @@ def build_extension(force: bool = False, verbose: bool = False) -> str:
     build_library()
     tmp = out + ".tmp"
     subprocess.run(["g++", "-shared", *objs, "-o", tmp, f"-L{torch_lib}", "-lc10", "-ltorch", "-ltorch_cpu",
-                    "-ltorch_python", "-lc10_cuda", "-ltorch_cuda", f"-L{PKG}", "-lyl_kvpath",
+                    "-ltorch_python", "-lc10_cuda", "-ltorch_cuda", f"-L{PKG}", "-lyl_kvpath", "-lyl_attention",
                     "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"], check=True)
     os.replace(tmp, out)
     return out

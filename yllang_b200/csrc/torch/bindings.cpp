@@ -74,11 +74,11 @@ PYBIND11_MODULE(_C, m) {
       .value("kLayerFirst", kLayerFirst)
       .export_values();
 
-  py::class_<MHAKVCache>(m, "MHAKVCache")
+  py::class_<MHAKVCache, std::shared_ptr<MHAKVCache>>(m, "MHAKVCache")
       .def(py::init([](int num_layers, int num_pages, int num_kv_heads, int head_dim, KVCacheLayout layout,
                        const std::string &device, py::object dtype, int page_size, bool zero_fill) {
              const auto st = torch::python::detail::py_object_to_dtype(dtype);
-             return std::make_unique<MHAKVCache>(num_layers, num_pages, num_kv_heads, head_dim, layout,
+             return std::make_shared<MHAKVCache>(num_layers, num_pages, num_kv_heads, head_dim, layout,
                                                  torch::Device(device), st, page_size, zero_fill);
            }),
            py::arg("num_layers"), py::arg("num_pages"), py::arg("num_kv_heads"), py::arg("head_dim"),
@@ -121,6 +121,37 @@ PYBIND11_MODULE(_C, m) {
   m.def("Make2DIndices", &Make2DIndices, py::arg("table"), py::arg("ranges"),
         "flat indices row + c, c in [col_start, col_end), of {row, col_start, col_end} ranges (int64, on the "
         "table's device)");
+
+  py::class_<AttentionContext, std::shared_ptr<AttentionContext>>(m, "AttentionContext")
+      .def(py::init([](const std::string &device, int64_t workspace_bytes) {
+             return std::make_shared<AttentionContext>(torch::Device(device), workspace_bytes);
+           }),
+           py::arg("device"), py::arg("workspace_bytes") = 256ll << 20)
+      .def(
+          "Plan",
+          [](AttentionContext &c, const BatchIndex &index, int num_qo_heads, int num_kv_heads, int head_dim,
+             int page_size, py::object dtype, std::optional<torch::Tensor> positions) {
+            c.Plan(index, num_qo_heads, num_kv_heads, head_dim, page_size,
+                   torch::python::detail::py_object_to_dtype(dtype), positions);
+          },
+          py::arg("index"), py::arg("num_qo_heads"), py::arg("num_kv_heads"), py::arg("head_dim"),
+          py::arg("page_size"), py::arg("dtype"), py::arg("positions") = py::none(),
+          "plan the step's paged attention from its page arrays (waits for the current stream)")
+      .def("IsDecode", &AttentionContext::IsDecode)
+      .def("Planned", &AttentionContext::Planned);
+  m.def("SetAttentionContext", &SetAttentionContext, py::arg("ctx"));
+  m.def("GetAttentionContext", &GetAttentionContext);
+  py::class_<Attention, std::shared_ptr<Attention>>(m, "Attention")
+      .def(py::init<int, int, int, int, std::shared_ptr<MHAKVCache>, QKNormRope>(), py::arg("layer_id"),
+           py::arg("num_qo_heads"), py::arg("num_kv_heads"), py::arg("head_dim"), py::arg("cache"),
+           py::arg("norm_rope") = QKNormRope{})
+      .def("Forward", py::overload_cast<const torch::Tensor &>(&Attention::Forward), py::arg("qkv_raw"),
+           "store this layer's K/V and attend over the pool, with the context set by SetAttentionContext")
+      .def("Forward", py::overload_cast<const torch::Tensor &, const AttentionContext &>(&Attention::Forward),
+           py::arg("qkv_raw"), py::arg("ctx"))
+      .def("LayerId", &Attention::LayerId)
+      .def("NumQoHeads", &Attention::NumQoHeads)
+      .def("NumKvHeads", &Attention::NumKvHeads);
 
   py::class_<KVCacheManager, std::shared_ptr<KVCacheManager>>(m, "KVCacheManager")
       .def(py::init([](int64_t num_pages, int64_t max_requests, int64_t max_pages_per_request, int page_size,

@@ -319,4 +319,94 @@ class BatchManager {
   torch::Tensor m_device_stage_;  // device int32 [3, capacity]
 };
 
+// ----------------------------------------------------------------------------
+// Attention layer: the reference's Attention (src/include/layers/attention.h:22-68),
+// whose Forward is a placeholder returning an empty tensor (:55), made real
+// for the paged pool.  Forward(qkv) splits one layer's projected rows
+// [N, (Hq + 2 Hk) * D] into q, k and v, stores k and v into the layer's pool
+// rows at the step's slots (with the per-head Q/K RMSNorm and rotary
+// embedding fused in when the layer has them), and runs flashinfer's paged
+// attention (third-party, unchanged) over the pool with the step's page
+// arrays: batch decode when every sequence adds one token, causal batch
+// prefill otherwise (query t of a sequence with L tokens after the step sits
+// at position L - n_new + t).  Hq and Hk are this GPU's heads: the model's
+// divided by the tensor-parallel size, as MHAKVCache divides its KV heads.
+// ----------------------------------------------------------------------------
+
+// One step's attention plan, shared by every layer of the step.
+class AttentionContext {
+ public:
+  explicit AttentionContext(torch::Device device, int64_t workspace_bytes = 256ll << 20);
+  ~AttentionContext();
+  AttentionContext(const AttentionContext &) = delete;
+  AttentionContext &operator=(const AttentionContext &) = delete;
+
+  // Once per step, after the index build.  Reads qo_indptr and kv_indptr
+  // back to the host (flashinfer plans its split of long sequences on the
+  // host), so it waits for the current stream.  positions [N] int32/int64
+  // are the new tokens' positions for the rotary embedding (needed only when
+  // a layer rotates q and k).
+  void Plan(const BatchIndex &index, int num_qo_heads, int num_kv_heads, int head_dim, int page_size,
+            torch::Dtype dtype, std::optional<torch::Tensor> positions = std::nullopt);
+
+  bool Planned() const { return m_planned_; }
+  bool IsDecode() const { return m_decode_; }
+  const BatchIndex &Index() const { return m_index_; }
+  const std::optional<torch::Tensor> &Positions() const { return m_positions_; }
+  int NumQoHeads() const { return m_qo_heads_; }
+  int NumKvHeads() const { return m_kv_heads_; }
+  int HeadDim() const { return m_head_dim_; }
+  int PageSize() const { return m_page_size_; }
+  torch::Dtype Dtype() const { return m_dtype_; }
+  torch::Device Device() const { return m_device_; }
+
+  // flashinfer's workspace and plan (for Attention::Forward).
+  struct Impl;
+  const Impl &Internal() const { return *m_impl_; }
+
+ private:
+  torch::Device m_device_;
+  std::unique_ptr<Impl> m_impl_;
+  BatchIndex m_index_;
+  std::optional<torch::Tensor> m_positions_;
+  bool m_planned_{false};
+  bool m_decode_{false};
+  int m_qo_heads_{0};
+  int m_kv_heads_{0};
+  int m_head_dim_{0};
+  int m_page_size_{0};
+  torch::Dtype m_dtype_{torch::kBFloat16};
+};
+
+// The context Forward(qkv) uses (the step's, set once per step by its driver).
+void SetAttentionContext(std::shared_ptr<AttentionContext> ctx);
+std::shared_ptr<AttentionContext> GetAttentionContext();
+
+class Attention {
+ public:
+  // norm_rope: per-head RMSNorm weights of q and k and/or a cos/sin cache for
+  // the rotary embedding (its positions come from the context); empty: the
+  // rows are stored and attended as given.
+  Attention(int layer_id, int num_qo_heads, int num_kv_heads, int head_dim, std::shared_ptr<MHAKVCache> cache,
+            QKNormRope norm_rope = {});
+
+  // qkv_raw [N, (Hq + 2 Hk) * D] (token rows may be strided); returns the
+  // attention output [N, Hq * D].
+  torch::Tensor Forward(const torch::Tensor &qkv_raw);
+  torch::Tensor Forward(const torch::Tensor &qkv_raw, const AttentionContext &ctx);
+
+  int LayerId() const { return m_layer_id_; }
+  int NumQoHeads() const { return m_qo_heads_; }
+  int NumKvHeads() const { return m_kv_heads_; }
+
+ private:
+  int m_layer_id_;
+  int m_qo_heads_;  // on this GPU
+  int m_kv_heads_;  // on this GPU
+  int m_head_dim_;
+  std::shared_ptr<MHAKVCache> m_cache_;
+  QKNormRope m_norm_rope_;
+  bool m_fused_;  // norm and/or rotary applied while storing
+};
+
 }  // namespace yllang
