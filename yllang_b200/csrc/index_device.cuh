@@ -37,7 +37,7 @@ struct IndexParams {
   int32_t slot64;
   FastDiv by_page;
   int64_t expected_tokens;  // step only: the store's N, checked against the sum of new_len (-1: no check)
-  int32_t beside_store;     // step only: the store may run beside this kernel; leave it room on each SM
+  int32_t beside_store;     // step only: the store may run beside this kernel (1), a long one (2); leave it room
 };
 
 // int64 words of shared scratch the scan needs: 2 x 32 warp totals, 2 block

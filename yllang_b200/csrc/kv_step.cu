@@ -316,7 +316,9 @@ extern "C" int yl_kv_step(const yl_step_args *a, cudaStream_t stream) {
       sp.p.self = SelfSlots{ix.prior_len, ix.new_len, ix.page_table, ix.table_index, ix.page_table_stride,
                             ix.num_pages, ix.batch, ix.page_size, ix.max_pages_per_row, ix.num_table_rows,
                             ix.slot64, ix.by_page};
-      ix.beside_store = 1;
+      const uint64_t store_bytes = 4ull * static_cast<uint64_t>(s.num_layers) *
+                                   static_cast<uint64_t>(s.num_tokens) * static_cast<uint64_t>(s.row_bytes);
+      ix.beside_store = store_bytes >= (48ull << 20) ? 2 : 1;
     }
     rc = launch_index(ix, stream);
     if (rc != YL_OK) return rc;

@@ -119,6 +119,11 @@ __global__ void __launch_bounds__(256) store_decode_kernel(const __grid_constant
     pl += R;
     if (pl < end) load(pl);
   }
+  // Computing its own slots, this grid never waited for the index build it
+  // was launched behind; wait before exiting, so that its completion implies
+  // the index build's (a kernel launched as its programmatic dependent, such
+  // as the next step's index build, relies on that order).
+  if (self) pdl_wait();
 }
 
 // TMA path: one CTA per SM stages its rows in shared memory.  The CTA owns a
