@@ -392,3 +392,18 @@ def test_device_error_names_and_debug_mode_default_off():
         assert C.DeviceErrorNames(bits) == want
     if not os.environ.get("YLLANG_CHECK_DEVICE_ERRORS"):
         assert not yl.ops.CHECK_DEVICE_ERRORS and not C.DeviceErrorChecksEnabled()
+
+
+def test_attention_library_exports_every_declared_symbol():
+    """include/yl_attention.h declares the C entry points of
+    libyl_attention.so; the library exports exactly those (its C++ bridge
+    functions are exported C++ symbols, not yl_*)."""
+    text = open(os.path.join(ROOT, "include", "yl_attention.h")).read()
+    declared = sorted(set(re.findall(r"YL_API\s+[\w\s\*]*?\b(yl_\w+)\s*\(", text)))
+    lib = os.path.join(ROOT, "yllang_b200", "libyl_attention.so")
+    out = subprocess.run(["nm", "-D", "--defined-only", lib], capture_output=True, text=True, check=True)
+    assert sorted(set(re.findall(r" T (yl_\w+)", out.stdout))) == declared
+    f = ctypes.CDLL(lib).yl_paged_decode_attention_noalloc
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    assert f(None, None) == -1  # YL_ERR_NULL_ARG, checked on the host before any launch

@@ -78,14 +78,16 @@ def build_attention(force: bool = False, verbose: bool = False) -> str:
     paged prefill kernels for sm_100a behind csrc/torch/attention_fi.h (no
     torch dependency; used by the front end's Attention)."""
     src = os.path.join(CSRC, "torch", "attention_fi.cu")
-    deps = [src, os.path.join(CSRC, "torch", "attention_fi.h")]
+    noalloc = os.path.join(CSRC, "torch", "attention_noalloc.cu")
+    deps = [src, noalloc, os.path.join(CSRC, "torch", "attention_fi.h"), os.path.join(INCLUDE, "yl_attention.h")]
     if not force and not _stale(ATTN_LIB, deps):
         return ATTN_LIB
     fi = _flashinfer_data()
     tmp = ATTN_LIB + ".tmp"
     cmd = [_nvcc(), "-std=c++17", "-O3", *GENCODE, "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler",
            "-fPIC,-fvisibility=hidden", "-shared", f"-I{fi}/cccl/libcudacxx/include", f"-I{fi}/include",
-           f"-I{fi}/cutlass/include", f"-I{fi}/spdlog/include", "-diag-suppress=20012,177,550", src, "-o", tmp]
+           f"-I{fi}/cutlass/include", f"-I{fi}/spdlog/include", f"-I{INCLUDE}", "-diag-suppress=20012,177,550",
+           src, noalloc, "-o", tmp]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
