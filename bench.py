@@ -60,7 +60,11 @@ FALLBACK_HBM_GBS = 6650.0
 # capture of three consecutive steps with caches left warm between them (so
 # each launch's DRAM writes include the write-back of the lines the previous
 # launch left dirty in L2); keyed by (workload, ranks).
-STEP_TRAFFIC_NCU: dict = {}
+STEP_TRAFFIC_NCU: dict = {
+    # store_decode_kernel + build_index_kernel of one decode step (256
+    # sequences, 32 layers), mean of the capture's steps 2 and 3
+    ("llama3_decode", 1): 66_239_872,
+}
 # Device-side delay queued ahead of each timed region (seconds at the maximum
 # SM clock): the host enqueues the graphs while the GPU spins, so the start
 # event is taken with the timed work already queued.

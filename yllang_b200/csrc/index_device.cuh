@@ -329,8 +329,11 @@ __device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, cons
 // warps of the grid (wps = warps in the grid / B, 1 to 8; warp part q of a
 // sequence takes its pages q*32 + lane + 32*wps*k), kSeqCopyUnroll pages per
 // lane in flight; no search.  For batches with more pages than threads,
-// where the per-element search's instructions dominate.
-constexpr int kSeqCopyUnroll = 4;
+// where the per-element search's instructions dominate.  Eight pages per lane
+// (four before) took one rank's decode step at 2,048 sequences from 21.5 to
+// 20.4 us and Qwen2-72B decode at one head per GPU from 14.0 to 13.7 us;
+// sixteen lost on the latter (16.1 us).
+constexpr int kSeqCopyUnroll = 8;
 __device__ inline void fill_kv_by_sequence(const IndexParams &p, const int32_t *kvp, int32_t n_idx) {
   const int lane = threadIdx.x & 31;
   const int warps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
