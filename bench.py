@@ -437,11 +437,6 @@ def launches_per_step(wl: Workload) -> int:
     """Kernels of this project one timed step launches (see yl_kv_step)."""
     b = wl.b0
     index_launches = 2 if b.batch > 16384 else 1
-    mode = os.environ.get("YL_STEP_MODE", "pdl")
-    if not wl.fused:
-        return index_launches + 1
-    if mode == "fused" and b.batch <= 4096:
-        return 1
     return index_launches + 1
 
 
@@ -800,7 +795,8 @@ def run_ours(args, world, rank, local):
         "config": dict(desc, parallelism=(f"replicas x{world}" if args.replicas else f"kv-head shard x{world}")
                        if world > 1 else ("single GPU" if shape_world == 1
                                           else f"one rank of a kv-head shard x{shape_world}, alone"),
-                       path=(f"yl_kv_step ({os.environ.get('YL_STEP_MODE', 'pdl')})" if wl.fused
+                       path=(("yl_kv_step (serial)" if os.environ.get("YL_STEP_MODE") == "serial"
+                              else "yl_kv_step (index build and store as programmatic dependents)") if wl.fused
                              else "build_index + store_kv_cache"),
                        l2=f"inputs rotate over {wl.R} sets ({wl.R * wl.per_set / 1e6:.0f} MB > 2 x L2), "
                           "distinct destination slots per set"),

@@ -179,13 +179,24 @@ typedef struct yl_index_args {
   uint32_t *error_word;         /* optional device word for YL_DEVERR_* bits    */
 } yl_index_args;
 
+/*
+ * Stream order: the index kernel is launched as a programmatic dependent of
+ * the kernel before it on the stream (its blocks may be placed while that
+ * kernel drains) and waits for that kernel to complete before it reads any
+ * input, so the call observes every earlier write on the stream, as a plain
+ * launch does.  (A preceding kernel that was itself launched as a
+ * programmatic dependent must, as that contract requires of it, wait for its
+ * own predecessor before completing.)
+ */
 YL_API int yl_build_index(const yl_index_args *args, cudaStream_t stream);
 
 /*
  * Step: yl_build_index(&index) followed by yl_kv_store of every layer with
- * slots = index.slot_mapping, fused into one launch when the batch has at
- * most 4096 sequences and the rows have a 16-byte fast shape (else the two
- * launches run back to back).  The result is identical to the two calls.
+ * slots = index.slot_mapping, as two launches that overlap: the store starts
+ * loading its K/V rows while the index build runs, and for a decode batch
+ * (store.num_tokens == batch_size, every new_len 1) computes its slots
+ * itself instead of waiting for them.  The result is identical to the two
+ * calls.
  * This is one serving step of the reference's path: the per-step index work
  * of BatchManager::NextBatch (src/include/batch/batch_manager.h:97-112)
  * followed by MHAKVCache::StoreKV (src/include/kvcache/mha_kvcache.h:76-86)

@@ -2,7 +2,8 @@
 
 Every wait of a bulk-copy kernel on its own copies is bounded (2 s of
 %globaltimer).  YL_BULK_WAIT_LIMIT_NS lowers the first wait of each round in
-the store's and the step's bulk-copy kernels; at 1 ns it gives up while the
+the store's bulk-copy kernel (YL_STORE_ENGINE=tma, on its own and as the
+step's store); at 1 ns it gives up while the
 round's rows are still landing, on a 67 MB store where HBM keeps most copies
 in flight for microseconds.  The kernel must then set YL_DEVERR_TIMEOUT, let
 its copies land (its second wait keeps the full bound), store nothing it has
@@ -33,8 +34,9 @@ i32 = dict(dtype=torch.int32, device=dev)
 
 def case(batch):
     # decode steps of 32 layers x 2 KB rows; at 1,024 sequences every CTA of
-    # the step's bulk-copy kernel stages its rows over several rounds, so some
-    # round's first wait starts while its copies are in flight
+    # the bulk-copy store behind the step's index build stages its rows over
+    # several rounds, so some round's first wait starts while its copies are
+    # in flight
     b = workloads.llama3_decode(num_pages=8192, batch=batch)
     E = b.kv_heads * b.head_dim
     k = torch.randn(b.layers, b.tokens, E, generator=g, device=dev).to(torch.bfloat16)
@@ -93,7 +95,7 @@ print("bulk wait timeouts ok")
 def test_bulk_copy_waits_time_out_cleanly(cuda):
     import torch
     torch.cuda.empty_cache()  # the child allocates 35 GB
-    env = dict(os.environ, YL_BULK_WAIT_LIMIT_NS="1", YL_STORE_ENGINE="tma", YL_STEP_MODE="tma")
+    env = dict(os.environ, YL_BULK_WAIT_LIMIT_NS="1", YL_STORE_ENGINE="tma")
     r = subprocess.run([sys.executable, "-c", CHILD], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "bulk wait timeouts ok" in r.stdout

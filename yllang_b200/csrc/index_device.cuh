@@ -1,5 +1,5 @@
-// Device side of the batch index build shared by the index kernels
-// (index_build.cu) and the fused step kernel (kv_step.cu).
+// Device side of the batch index build (index_build.cu; the step's decode
+// store, store_device.cuh, follows the same slot rules).
 //
 // The per-sequence page and token counts are exclusive-scanned into
 // kv_indptr / qo_indptr offsets (in shared memory, or in the outputs for very
@@ -220,32 +220,9 @@ __device__ __forceinline__ int find_seq32(const int32_t *off, int n, int32_t e, 
 
 __device__ __forceinline__ int pow2_floor(int n) { return n > 0 ? 1 << (31 - __clz(n)) : 0; }
 
-// Largest i in [lo, hi) with off[i] <= e, given off[lo] <= e < off[hi].
-__device__ __forceinline__ int find_seq_in(const int32_t *off, int lo, int hi, int64_t e) {
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (off[mid] <= e) lo = mid; else hi = mid;
-  }
-  return lo;
-}
-
-// Largest i in [0, n) with off[i] <= e, given off[0] <= e < off[n].
-__device__ __forceinline__ int find_seq(const int32_t *off, int n, int64_t e) { return find_seq_in(off, 0, n, e); }
-
-
 __device__ __forceinline__ void write_slot(const IndexParams &p, int64_t t, int64_t slot) {
   if (p.slot64) static_cast<int64_t *>(p.slot_mapping)[t] = slot;
   else static_cast<int32_t *>(p.slot_mapping)[t] = static_cast<int32_t>(slot);
-}
-
-// kv_indices[e] for one element e < kv_indptr[B] (the fused step kernels).
-__device__ __forceinline__ void kv_index_elem(const IndexParams &p, const int32_t *kvp, int64_t e) {
-  const int i = find_seq(kvp, p.batch, e);
-  const int64_t col = e - kvp[i];
-  const int32_t row = p.table_index ? p.table_index[i] : i;
-  const int32_t page = p.page_table[static_cast<int64_t>(row) * p.page_table_stride + col];
-  if (p.num_pages > 0 && (page < 0 || page >= p.num_pages)) raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
-  p.kv_indices[e] = page;
 }
 
 // Slot of position `pos` of sequence i, or -1 when it has none (the position
@@ -262,13 +239,6 @@ __device__ __forceinline__ int64_t slot_at(const IndexParams &p, const int32_t *
   if (in_range && (p.slot64 || s <= INT_MAX)) return s;
   raise_deverr(p.error_word, YL_DEVERR_PAGE_RANGE);
   return -1;
-}
-
-// Slot of new token t < qo_indptr[B] (the token's sequence found by search).
-__device__ __forceinline__ int64_t token_slot(const IndexParams &p, const int32_t *kvp, const int32_t *qop,
-                                              int64_t t) {
-  const int i = find_seq(qop, p.batch, t);
-  return slot_at(p, kvp, i, static_cast<int64_t>(max(p.prior_len[i], 0)) + (t - qop[i]));
 }
 
 // Phase C for the elements [begin, end) of [kv_indices | slot_mapping]: one
@@ -434,28 +404,7 @@ __device__ __forceinline__ void fill_block_share(const IndexParams &p, const int
     fill_range<U>(p, kvp, qop, static_cast<int32_t>(n_idx), static_cast<int32_t>(begin), static_cast<int32_t>(end));
 }
 
-// kv_indices share of this block when the slots of tokens [0, slot_begin) are
-// written elsewhere (the fused step kernel writes them while it stores); the
-// slot entries [slot_begin, slot capacity) are set to -1 here.
-__device__ __forceinline__ void fill_kv_share(const IndexParams &p, const int32_t *kvp, int64_t slot_begin,
-                                              bool report) {
-  int64_t n_idx = p.kv_indices ? kvp[p.batch] : 0;
-  if (n_idx > p.indices_cap) {
-    if (report && threadIdx.x == 0) raise_deverr(p.error_word, YL_DEVERR_INDICES_CAP);
-    n_idx = p.indices_cap;
-  }
-  const int64_t tail = p.slot_mapping && p.slots_cap > slot_begin ? p.slots_cap - slot_begin : 0;
-  const int64_t work = n_idx + tail;
-  const int64_t chunk = (work + gridDim.x - 1) / gridDim.x;
-  const int64_t begin = static_cast<int64_t>(blockIdx.x) * chunk;
-  const int64_t end = min(begin + chunk, work);
-  for (int64_t e = begin + threadIdx.x; e < end; e += blockDim.x) {
-    if (e < n_idx) kv_index_elem(p, kvp, e);
-    else write_slot(p, slot_begin + (e - n_idx), -1);
-  }
-}
-
-// Host halves of yl_build_index (index_build.cu), shared with the fused step:
+// Host halves of yl_build_index (index_build.cu), shared with the step:
 // prepare_index validates the arguments and fills the kernel parameters,
 // launch_index launches the index kernels.
 int prepare_index(const yl_index_args *a, IndexParams &p);

@@ -1,5 +1,5 @@
-// Device side of the K/V row copy shared by the store kernel (kv_store.cu) and
-// the fused step kernel (kv_step.cu).
+// Device side of the K/V row copy of the store kernels (kv_store.cu), which
+// the step (kv_step.cu) launches behind its index build.
 //
 // Rows are enumerated plane-major: row r in [0, 2 * L * N) is token r % N of
 // plane r / N, plane = 2 * layer + {0: K, 1: V}.  A group of G lanes copies one
@@ -268,7 +268,7 @@ inline bool dispatch_row_shape(int64_t row_bytes, int w, F &&f) {
 int fast_vector_bytes();
 
 // Host halves of the entry points (kv_store.cu, index_build.cu), shared with
-// the fused step (kv_step.cu).  `prepare_*` validate the arguments and fill
+// the step (kv_step.cu).  `prepare_*` validate the arguments and fill
 // the kernel parameters; `launch_*` launch the separate kernels.
 struct StorePlan {
   StoreParams p;
