@@ -141,6 +141,46 @@ def test_cpp_attention_with_qk_norm(cuda):
         torch.testing.assert_close(out[i].view(Hq, D).float(), want[0], atol=ATOL, rtol=RTOL)
 
 
+def _rope_neox(x, cs, positions):
+    """Rotate-half rotary embedding by the [max_position, D] cos / sin cache."""
+    D = x.shape[-1]
+    c = cs[positions.long(), :D // 2][:, None, :]
+    s = cs[positions.long(), D // 2:][:, None, :]
+    x1, x2 = x[..., :D // 2].float(), x[..., D // 2:].float()
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def test_cpp_attention_with_norm_and_rotary_from_the_context(cuda):
+    """Q/K RMSNorm then the rotary embedding at the step's positions (handed
+    to the context by the step's driver), stored and attended."""
+    Hq, Hk, D, ps, P, eps = 16, 8, 128, 16, 1024, 1e-6
+    rng = np.random.default_rng(13)
+    prior = rng.integers(10, 200, 8).astype(np.int32)
+    fresh = np.ones(8, np.int32)
+    cache, hist_k, hist_v, idx, qkv = _setup(cuda, prior, fresh, Hq, Hk, D, ps, P, layers=1, layer=0, seed=4)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    opts = C.QKNormRope()
+    opts.q_weight = (1 + 0.1 * torch.randn(D, generator=g, device=cuda)).to(torch.bfloat16)
+    opts.k_weight = (1 + 0.1 * torch.randn(D, generator=g, device=cuda)).to(torch.bfloat16)
+    opts.eps = eps
+    opts.cos_sin_cache = yl.rope_cos_sin_cache(4096, D, theta=1e6, device=cuda)
+    positions = torch.from_numpy(prior.astype(np.int64)).to(cuda)  # the new token's position
+    ctx = C.AttentionContext("cuda")
+    ctx.Plan(idx, Hq, Hk, D, ps, torch.bfloat16, positions)
+    out = C.Attention(0, Hq, Hk, D, cache, opts).Forward(qkv, ctx)
+    torch.cuda.synchronize()
+    q, k, v = _split(qkv, Hq, Hk, D)
+    qr = _rope_neox(_rmsnorm(q, opts.q_weight, eps), opts.cos_sin_cache, positions).to(torch.bfloat16)
+    kr = _rope_neox(_rmsnorm(k, opts.k_weight, eps), opts.cos_sin_cache, positions).to(torch.bfloat16)
+    for i in range(8):
+        want = _attend(qr[i:i + 1], torch.cat([hist_k[i], kr[i:i + 1]]), torch.cat([hist_v[i], v[i:i + 1]]), 1)
+        torch.testing.assert_close(out[i].view(Hq, D).float(), want[0], atol=ATOL, rtol=RTOL)
+    ctx_no_pos = C.AttentionContext("cuda")
+    ctx_no_pos.Plan(idx, Hq, Hk, D, ps, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="positions"):
+        C.Attention(0, Hq, Hk, D, cache, opts).Forward(qkv, ctx_no_pos)
+
+
 def test_cpp_attention_refusals(cuda):
     cache = C.MHAKVCache(1, 64, 8, 128, C.KVCacheLayout.kLayerFirst, "cuda", torch.bfloat16, 16)
     with pytest.raises(RuntimeError, match="layer_id"):

@@ -87,6 +87,33 @@ struct FastDiv {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// Launch `kernel` as a programmatic dependent of the kernel before it on the
+// stream: its blocks may be placed while that kernel drains, which hides the
+// launch.  The kernel must call pdl_wait() before it touches memory an
+// earlier kernel may have written (for a normal launch the wait returns at
+// once), so stream order is kept.  Returns a yl_status.
+template <typename... KArgs, typename... Args>
+inline int launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            const char *what, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return YL_ERR_CUDA;
+  }
+  return check_launch(what);
+}
+
 __device__ __forceinline__ void raise_deverr(uint32_t *word, uint32_t bit) {
   if (word != nullptr) atomicOr(word, bit);
 }

@@ -165,6 +165,6 @@ extern "C" int yl_gather_rows(const yl_gather_args *a, cudaStream_t stream) {
   const uint64_t rows_per_block = static_cast<uint64_t>(256 / group) * rows;
   const uint64_t want = (static_cast<uint64_t>(p.n) + rows_per_block - 1) / rows_per_block;
   const uint64_t cap = static_cast<uint64_t>(sm_count()) * blocks_per_sm(reinterpret_cast<const void *>(fn), 0);
-  fn<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(p);
-  return check_launch("yl_gather_rows launch");
+  return launch_dependent(fn, dim3(static_cast<unsigned>(want < cap ? want : cap)), dim3(256), 0, stream,
+                          "yl_gather_rows launch", p);
 }

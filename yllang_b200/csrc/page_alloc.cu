@@ -327,8 +327,7 @@ extern "C" int yl_reserve_pages(const yl_reserve_args *a, cudaStream_t stream) {
   PoolParams p{a->pool.free_pages, a->pool.free_count, a->pool.capacity, a->page_table, a->prior_len, a->new_len,
                a->table_index, a->page_table_stride, a->num_table_rows, a->max_pages_per_row, a->page_size,
                a->batch_size, a->error_word};
-  reserve_pages_kernel<<<1, kPoolThreads, 0, stream>>>(p);
-  return check_launch("yl_reserve_pages launch");
+  return launch_dependent(reserve_pages_kernel, dim3(1), dim3(kPoolThreads), 0, stream, "yl_reserve_pages launch", p);
 }
 
 extern "C" int yl_release_pages(const yl_release_args *a, cudaStream_t stream) {
@@ -348,6 +347,5 @@ extern "C" int yl_release_pages(const yl_release_args *a, cudaStream_t stream) {
   PoolParams p{a->pool.free_pages, a->pool.free_count, a->pool.capacity, a->page_table, a->num_tokens, nullptr,
                a->rows, a->page_table_stride, a->num_table_rows, a->max_pages_per_row, a->page_size,
                a->num_release, a->error_word};
-  release_pages_kernel<<<1, kPoolThreads, 0, stream>>>(p);
-  return check_launch("yl_release_pages launch");
+  return launch_dependent(release_pages_kernel, dim3(1), dim3(kPoolThreads), 0, stream, "yl_release_pages launch", p);
 }

@@ -763,14 +763,14 @@ extern "C" int yl_qkv_norm_rope_store(const yl_qkv_store_args *a, cudaStream_t s
         cudaSuccess)
       return check_launch("yl_qkv_norm_rope_store: shared memory attribute");
     const uint64_t grid = tiles < sms ? tiles : sms;
-    shape.fn<<<static_cast<unsigned>(grid), 32 * (1 + shape.cw), smem, stream>>>(p);
-    return check_launch("yl_qkv_norm_rope_store launch");
+    return launch_dependent(shape.fn, dim3(static_cast<unsigned>(grid)), dim3(32 * (1 + shape.cw)), smem, stream,
+                            "yl_qkv_norm_rope_store launch", p);
   }
   const Kernel fn = engine == 1 ? ks.big : ks.small;
   set_chunks(p, engine == 1 ? ks.g_big : 2);
   p.items = static_cast<uint32_t>(a->num_tokens * static_cast<int64_t>(p.chunks));
   const uint64_t want = (static_cast<uint64_t>(p.items) + 7) / 8;  // 8 warps per block
   const uint64_t cap = sms * blocks_per_sm(reinterpret_cast<const void *>(fn), 0);
-  fn<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(p);
-  return check_launch("yl_qkv_norm_rope_store launch");
+  return launch_dependent(fn, dim3(static_cast<unsigned>(want < cap ? want : cap)), dim3(256), 0, stream,
+                          "yl_qkv_norm_rope_store launch", p);
 }

@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(kRangeThreads) make_2d_indices_kernel(const __
   const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * (kRangeThreads / 32) + warp;
   const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * (kRangeThreads / 32) * kWarpTile;
   int64_t carry = 0;  // indices of the chunks before this one
+  pdl_wait();  // the ranges may be written by the kernel just before this one
   for (int c0 = 0; c0 < p.num_ranges; c0 += kRangeThreads) {
     const int n = min(kRangeThreads, p.num_ranges - c0);
     int64_t len = 0, start = 0;
@@ -149,6 +150,6 @@ extern "C" int yl_make_2d_indices(const yl_ranges_args *a, cudaStream_t stream) 
   const int64_t want = (a->indices_capacity + per_block - 1) / per_block;
   const int64_t cap = 2ll * sm_count();
   const unsigned grid = static_cast<unsigned>(want < 1 ? 1 : (want < cap ? want : cap));
-  make_2d_indices_kernel<<<grid, kRangeThreads, 0, stream>>>(p);
-  return check_launch("yl_make_2d_indices launch");
+  return launch_dependent(make_2d_indices_kernel, dim3(grid), dim3(kRangeThreads), 0, stream,
+                          "yl_make_2d_indices launch", p);
 }
