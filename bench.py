@@ -299,6 +299,23 @@ def per_launch_us(R, launches, n, reps=4):
     return us
 
 
+def size_matched_copy_us(dev, nbytes: int, n: int = 64) -> float:
+    """Device time (us) of a plain contiguous torch copy of nbytes / 2 bytes
+    into another buffer (nbytes of reads + writes, the step's algorithmic
+    volume), sources and destinations rotating past L2, back to back in a
+    CUDA graph: what moving the same bytes costs with no scatter and no index
+    build, at this transfer size."""
+    half = max(nbytes // 16, 1)  # 8-byte elements: torch's copy then moves wide vectors
+    R = max(2, math.ceil(2.2 * L2_BYTES / (8 * half)))
+    src = [torch.empty(half, dtype=torch.int64, device=dev) for _ in range(R)]
+    dst = [torch.empty(half, dtype=torch.int64, device=dev) for _ in range(R)]
+    for t in src:
+        t.fill_(1)
+    us = per_launch_us(R, lambda r: [lambda: dst[r].copy_(src[r])], n)
+    del src, dst
+    return us
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -756,6 +773,7 @@ def run_ours(args, world, rank, local):
     layer_us = reduce_max(per_launch_us(wl.R, lambda r: [(lambda l: (lambda: wl.steps[r].store_layer(
         l, wl.k_pool, wl.v_pool, wl.err)))(layer) for layer in range(L)], n_layer), world) / L
     wl.check_err("in the per-layer store timing")
+    copy_us = reduce_max(size_matched_copy_us(dev, m["step_bytes"]), world)
     e2e = None
     if not args.no_e2e:
         if wl.per_set <= 4e9:
@@ -819,6 +837,9 @@ def run_ours(args, world, rank, local):
                                       "frac": round(store_gbs / peak, 4),
                                       "algorithmic_bytes_per_launch": m["store_bytes"],
                                       "timing": "the all-layer store alone, back-to-back launches in one graph"}},
+        "size_matched_copy": {"us": round(copy_us, 3), "step_over_copy": round(m["step_us"] / copy_us, 3),
+                              "what": "a contiguous device copy moving the step's algorithmic bytes (half read, "
+                                      "half written), inputs past L2, back to back in a graph"},
         "per_layer_store": {"launches_per_step": L, "us_per_launch": round(layer_us, 3),
                             "gbs": round(m["store_bytes"] / L / (layer_us * 1e-6) / 1e9, 1)},
         "gpu_launches": K * m["launches_per_step"],
