@@ -267,8 +267,16 @@ __device__ inline void fill_range(const IndexParams &p, const int32_t *kvp, cons
   for (int32_t e0 = begin + static_cast<int32_t>(threadIdx.x); e0 < kv_end; e0 += U * step) {
     int seq[U];
     int32_t page[U];
+    // one search for the first element; a later element in the same
+    // sequence (long rows: page size 1, long contexts) needs one shared-memory
+    // load instead of its own search, and the other searches stay independent
+    const int s0 = e0 < kv_end ? find_seq32(kvp, p.batch, e0, top) : -1;
+    const int32_t s0_end = s0 >= 0 ? kvp[s0 + 1] : 0;
 #pragma unroll
-    for (int u = 0; u < U; ++u) seq[u] = e0 + u * step < kv_end ? find_seq32(kvp, p.batch, e0 + u * step, top) : -1;
+    for (int u = 0; u < U; ++u) {
+      const int32_t e = e0 + u * step;
+      seq[u] = e >= kv_end ? -1 : (e < s0_end ? s0 : find_seq32(kvp, p.batch, e, top));
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (seq[u] >= 0) {
