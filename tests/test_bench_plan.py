@@ -43,3 +43,17 @@ def test_plan_rotation_exceeds_l2():
 def test_head_split_must_be_even():
     with pytest.raises(Exception):
         bench.make_batches("llama3_decode", 3, 150e9, 1)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_reference_arm_times_the_whole_job(world):
+    """At N ranks the reference arm (rank 0's host cores) runs the whole job
+    of our arm: the global batch of all ranks with every KV head, i.e. N
+    times one rank's store bytes for the weak-scaling decode, and the same
+    batch with every head for the strong-scaling Qwen2-72B decode."""
+    whole, desc = bench.make_batches("llama3_decode", world, 150e9, 1, whole_job=True)
+    rank, _ = bench.make_batches("llama3_decode", world, 150e9, 1)
+    assert whole[0].batch == 256 * world and whole[0].kv_heads == 8 and desc["global_batch"] == 256 * world
+    assert whole[0].tokens * whole[0].row_bytes == world * rank[0].tokens * rank[0].row_bytes
+    q, _ = bench.make_batches("qwen72b_decode", world, 150e9, 1, whole_job=True)
+    assert q[0].batch == 512 and q[0].kv_heads == 8
