@@ -23,9 +23,9 @@
 #include <cuda_runtime.h>
 
 #include <climits>
-#include <string>
 #include <cstdint>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
