@@ -26,6 +26,13 @@
  * row too short, an output buffer too small) skip the offending element and
  * set a bit in the caller's optional device error word (see YL_DEVERR_*);
  * kernels never trap.
+ *
+ * Stream order is that of plain launches.  Most kernels here are launched as
+ * programmatic dependents of the kernel before them on the stream, which
+ * lets their blocks be placed while that kernel drains; each waits for that
+ * kernel to complete before touching memory it may have written.  The one
+ * exception, yl_kv_store, is a plain launch (it starts loading its K/V rows
+ * at once).
  */
 #ifndef YL_KVPATH_H_
 #define YL_KVPATH_H_
