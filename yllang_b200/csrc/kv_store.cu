@@ -252,6 +252,7 @@ __global__ void __launch_bounds__(256) store_rows_generic_kernel(const __grid_co
 using StoreKernel = void (*)(StoreParams);
 
 using DecodeKernel = void (*)(StoreParams, uint32_t, uint32_t);
+constexpr uint64_t kDecodeUnitBytes = 20 * 1024;  // rows one lane group of the decode store takes at most
 struct StoreVariant {
   StoreKernel fn;
   int group;  // lanes per row
@@ -468,12 +469,14 @@ int launch_store(const StorePlan &plan, int64_t row_bytes, bool slot64, cudaStre
     const uint64_t resident = static_cast<uint64_t>(sm_count()) *
                               blocks_per_sm(reinterpret_cast<const void *>(var.dec), 0) * groups;
     uint64_t chunk = R * ((planes * n + resident * R - 1) / (resident * R));
-    // at most 4 iterations per unit: in a long store (80 layers) the CTAs
-    // that start late, behind the index build's blocks, would otherwise carry
-    // long runs past everyone else (Qwen2-72B decode, 8 heads: 60.8 -> 58.2
-    // us per step with 8-plane runs instead of 18; a 32-layer decode step
-    // keeps its 4-plane runs)
-    if (chunk > 4 * R) chunk = 4 * R;
+    // at most kDecodeUnitBytes of rows per unit: in a long store (80 layers)
+    // the CTAs that start late, behind the index build's blocks, would
+    // otherwise carry long runs past everyone else (Qwen2-72B decode, 8 heads:
+    // 60.8 -> ~58 us per step with 10-plane runs of 2 KB rows instead of 18;
+    // a 32-layer decode step keeps its 4-plane runs, Qwen2-72B at 4 heads per
+    // GPU its 20 planes of 1 KB)
+    const uint64_t cap_planes = kDecodeUnitBytes / static_cast<uint64_t>(row_bytes) / R * R;
+    if (cap_planes >= R && chunk > cap_planes) chunk = cap_planes;
     const uint64_t max_chunk = (planes + R - 1) / R * R;
     if (chunk > max_chunk) chunk = max_chunk;
     const uint64_t units = (planes + chunk - 1) / chunk * n;
